@@ -1,0 +1,412 @@
+"""CPU restatement of NanoInfer's per-token decoder elementwise path.
+
+TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``): the checker for the CUDA
+kernels, never the product path.
+
+Every floating-point function below spells out the rounding order of the
+reference's eager PyTorch code with CPU tensor arithmetic (fp32 math, explicit
+bf16/fp16 rounding points). Byte and index work (paged-KV store/gather,
+embedding rows, DeepStack row selection) is restated in numpy on integer views
+of the tensors, so it is bit-exact by construction. Citations are
+``file:line`` inside the NanoInfer project.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+__all__ = [
+    "add_rms_norm",
+    "rms_norm",
+    "text_rms_norm",
+    "add_text_rms_norm",
+    "silu_and_mul",
+    "silu_and_mul_fp32",
+    "rope_cos_sin_cache",
+    "apply_rope",
+    "mrope_inv_freq",
+    "mrope_cos_sin",
+    "mrope_select",
+    "apply_mrope",
+    "mrope_forward",
+    "paged_store",
+    "paged_gather",
+    "embedding",
+    "add_deepstack_rows",
+    "qk_norm_rope_store",
+    "qwen3_vl_fused_layer",
+]
+
+
+def _round(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    return t.to(dtype)
+
+
+# --------------------------------------------------------------------------- norms
+
+
+def add_rms_norm(x, residual, weight, eps):
+    """Fused residual add + RMSNorm.
+
+    Follows ``nanovllm/layers/layernorm.py:28-40`` (``add_rms_forward``): the sum
+    is kept in fp32 for the statistics, the new residual is that sum rounded to
+    the activation dtype, the normalised value is rounded before the weight
+    multiply, and the weight multiply rounds once more (``mul_`` on the
+    rounded tensor).
+    """
+    dtype = x.dtype
+    s = x.float() + residual.float()
+    res_out = _round(s, dtype)
+    var = s.pow(2).mean(dim=-1, keepdim=True)
+    n = _round(s * torch.rsqrt(var + eps), dtype)
+    y = _round(n.float() * weight.float(), dtype)
+    return y, res_out
+
+
+def rms_norm(x, weight, eps):
+    """RMSNorm without residual: ``nanovllm/layers/layernorm.py:16-26``.
+
+    Output is a new tensor (``x.float()`` copies), laid out contiguously.
+    """
+    dtype = x.dtype
+    xf = x.float()
+    var = xf.pow(2).mean(dim=-1, keepdim=True)
+    n = _round(xf * torch.rsqrt(var + eps), dtype)
+    return _round(n.float() * weight.float(), dtype).contiguous()
+
+
+def text_rms_norm(x, weight, eps):
+    """``Qwen3VLTextRMSNorm.forward``: ``nanovllm/models/qwen3_vl.py:74-79``.
+
+    ``weight * normalized.to(input_dtype)``: the product is taken in the
+    promoted dtype of the weight and the activation (bf16 x bf16 -> bf16,
+    fp32 weight -> fp32 output).
+    """
+    dtype = x.dtype
+    xf = x.float()
+    var = xf.pow(2).mean(-1, keepdim=True)
+    n = _round(xf * torch.rsqrt(var + eps), dtype)
+    out_dtype = torch.promote_types(weight.dtype, dtype)
+    return _round(weight.float() * n.float(), out_dtype).contiguous()
+
+
+def add_text_rms_norm(x, residual, weight, eps):
+    """Qwen3-VL residual add then text RMSNorm.
+
+    ``nanovllm/models/qwen3_vl.py:232-237``: ``hidden_states + residual`` is a
+    plain activation-dtype add (one rounding) and the norm then runs on the
+    rounded sum, unlike ``add_rms_norm`` which normalises the fp32 sum.
+    Returns ``(normed, rounded_sum)``.
+    """
+    s = _round(x.float() + residual.float(), x.dtype)
+    return text_rms_norm(s, weight, eps), s
+
+
+# --------------------------------------------------------------------------- activation
+
+
+def silu_and_mul(x):
+    """``SiluAndMul.forward`` as eager PyTorch runs it.
+
+    ``nanovllm/layers/activation.py:8-11``: ``silu`` rounds to the activation
+    dtype, the product rounds again.
+    """
+    gate, up = x.chunk(2, -1)
+    return F.silu(gate) * up
+
+
+def silu_and_mul_fp32(x):
+    """Single-rounding form: ``silu(gate) * up`` in fp32, rounded once.
+
+    This is what the reference's ``@torch.compile``d ``SiluAndMul`` computes on
+    GPU (inductor upcasts the fused expression to fp32).
+    """
+    gate, up = x.chunk(2, -1)
+    return _round(F.silu(gate.float()) * up.float(), x.dtype)
+
+
+# --------------------------------------------------------------------------- rotary
+
+
+def rope_cos_sin_cache(head_size, max_position, base):
+    """``RotaryEmbedding.__init__`` table: ``nanovllm/layers/rotary_embedding.py:29-35``.
+
+    Shape ``[max_position, 1, head_size]`` fp32: cos of the first half, sin of
+    the second half of the last dimension.
+    """
+    inv_freq = 1.0 / (base ** (torch.arange(0, head_size, 2, dtype=torch.float) / head_size))
+    t = torch.arange(max_position, dtype=torch.float)
+    freqs = torch.einsum("i,j -> ij", t, inv_freq)
+    return torch.cat((freqs.cos(), freqs.sin()), dim=-1).unsqueeze_(1)
+
+
+def _rotate_neox_fp32(x, cos, sin):
+    # nanovllm/layers/rotary_embedding.py:6-14: fp32 math, one rounding at the end
+    half = x.shape[-1] // 2
+    xf = x.float()
+    x1, x2 = xf[..., :half], xf[..., half:]
+    y1 = x1 * cos - x2 * sin
+    y2 = x2 * cos + x1 * sin
+    return _round(torch.cat((y1, y2), dim=-1), x.dtype)
+
+
+def apply_rope(positions, query, key, cos_sin_cache):
+    """``RotaryEmbedding.forward``: ``nanovllm/layers/rotary_embedding.py:37-48``."""
+    cos_sin = cos_sin_cache[positions.long()]
+    half = cos_sin.shape[-1] // 2
+    cos, sin = cos_sin[..., :half], cos_sin[..., half:]
+    return _rotate_neox_fp32(query, cos, sin), _rotate_neox_fp32(key, cos, sin)
+
+
+def mrope_inv_freq(head_dim, base):
+    """``MultimodalRotaryEmbedding.__init__`` inverse frequencies.
+
+    ``nanovllm/layers/multimodal_rotary_embedding.py:70-86`` (built in fp32).
+    """
+    return 1.0 / (base ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+
+
+def mrope_cos_sin(positions, inv_freq, dtype):
+    """``MultimodalRotaryEmbedding.cos_sin``: ``multimodal_rotary_embedding.py:89-101``.
+
+    fp32 ``position * inv_freq``, duplicated to the full head dim, cos/sin in
+    fp32, then rounded to ``dtype``. Returns two ``[3, T, head_dim]`` tensors.
+    """
+    freqs = positions.to(torch.float32).unsqueeze(-1) * inv_freq.view(1, 1, -1)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return _round(emb.cos(), dtype), _round(emb.sin(), dtype)
+
+
+def mrope_select(values, sections, strategy):
+    """``_select_frequency_layout``: ``multimodal_rotary_embedding.py:120-147``.
+
+    ``values`` is ``[3, T, D]``; the result is ``[T, 1, D]``.
+
+    * ``chunked`` (Qwen2.5-VL): split the last dim into ``sections+sections``;
+      chunk ``i`` takes its values from axis ``i % 3``.
+    * ``interleaved`` (Qwen3-VL): on the first half, frequency ``j`` reads axis
+      1 when ``j % 3 == 1 and j < 3*sections[1]``, axis 2 when
+      ``j % 3 == 2 and j < 3*sections[2]``, else axis 0; the second half
+      repeats the first.
+    """
+    d = values.shape[-1]
+    if strategy == "chunked":
+        bounds = np.cumsum((0,) + tuple(sections) + tuple(sections))
+        parts = [values[i % 3, ..., bounds[i]:bounds[i + 1]] for i in range(6)]
+        selected = torch.cat(parts, dim=-1)
+    elif strategy == "interleaved":
+        half = d // 2
+        sel = values[0, ..., :half].clone()
+        for axis, offset in ((1, 1), (2, 2)):
+            idx = list(range(offset, sections[axis] * 3, 3))
+            sel[..., idx] = values[axis, ..., :half][..., idx]
+        selected = torch.cat((sel, sel), dim=-1)
+    else:
+        raise ValueError("multimodal rotary strategy must be 'chunked' or 'interleaved'")
+    return selected.unsqueeze(1)
+
+
+def _rotate_half(x):
+    half = x.shape[-1] // 2
+    return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+
+
+def apply_mrope(query, key, cos, sin, sections, strategy="chunked"):
+    """``apply_multimodal_rotary_emb``: ``multimodal_rotary_embedding.py:12-45``.
+
+    ``chunked``: fp32 math on the (already rounded) cos/sin, rounded once.
+    ``interleaved``: arithmetic in the tensors' own dtype, i.e. for bf16
+    ``round(round(q*c) + round(rotate_half(q)*s))``.
+    """
+    sc = mrope_select(cos, sections, strategy)
+    ss = mrope_select(sin, sections, strategy)
+    qd, kd = query.dtype, key.dtype
+    if strategy == "chunked":
+        q, k, sc, ss = query.float(), key.float(), sc.float(), ss.float()
+    else:
+        q, k = query, key
+    q_out = q * sc + _rotate_half(q) * ss
+    k_out = k * sc + _rotate_half(k) * ss
+    return _round(q_out, qd), _round(k_out, kd)
+
+
+def mrope_forward(positions, query, key, inv_freq, sections, strategy):
+    """``MultimodalRotaryEmbedding.forward``: ``multimodal_rotary_embedding.py:103-117``."""
+    cos, sin = mrope_cos_sin(positions, inv_freq, query.dtype)
+    return apply_mrope(query, key, cos, sin, sections, strategy)
+
+
+# --------------------------------------------------------------------------- byte / index work
+
+
+def _as_int_view(t: torch.Tensor) -> np.ndarray:
+    """Integer view of a CPU tensor's bytes (bit-exact copy semantics)."""
+    itype = {1: torch.int8, 2: torch.int16, 4: torch.int32, 8: torch.int64}[t.element_size()]
+    return t.contiguous().view(itype).numpy()
+
+
+def _from_int_view(a: np.ndarray, dtype: torch.dtype) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).view(dtype)
+
+
+def paged_store(key, value, key_cache, value_cache, slot_mapping):
+    """Paged-KV store: ``nanovllm/layers/paged_kv/pytorch_backend.py:26-38``.
+
+    For token ``i`` with ``slot_mapping[i] >= 0``, row ``i`` of key/value
+    (``kv_heads*head_dim`` elements) overwrites flat slot ``slot_mapping[i]`` of
+    the caches; ``-1`` skips the token, and every other slot keeps its bytes.
+    Returns new ``(key_cache, value_cache)`` tensors (inputs untouched).
+    """
+    nb, bs, h, d = key_cache.shape
+    slots = slot_mapping.numpy().astype(np.int64)
+    valid = slots >= 0
+    out = []
+    for src, cache in ((key, key_cache), (value, value_cache)):
+        c = _as_int_view(cache).reshape(nb * bs, h * d).copy()
+        s = _as_int_view(src).reshape(src.shape[0], h * d)
+        c[slots[valid]] = s[valid]
+        out.append(_from_int_view(c.reshape(nb, bs, h, d), cache.dtype))
+    return out[0], out[1]
+
+
+def paged_gather(cache, block_table, sequence_length):
+    """Paged-KV gather: ``nanovllm/layers/paged_kv/pytorch_backend.py:40-50``.
+
+    ``out[t] = cache[block_table[t // block_size], t % block_size]`` for
+    ``t < sequence_length``; result ``[sequence_length, kv_heads, head_dim]``.
+    """
+    nb, bs, h, d = cache.shape
+    req = (sequence_length + bs - 1) // bs
+    if req == 0:
+        return torch.empty((0, h, d), dtype=cache.dtype)
+    c = _as_int_view(cache)
+    ids = block_table.numpy()[:req].astype(np.int64)
+    rows = c[ids].reshape(req * bs, h, d)[:sequence_length]
+    return _from_int_view(rows, cache.dtype)
+
+
+def embedding(ids, weight):
+    """``VocabParallelEmbedding.forward`` at tp=1: ``nanovllm/layers/embed_head.py:34-42``.
+
+    Row gather ``weight[ids]``.
+    """
+    w = _as_int_view(weight)
+    return _from_int_view(w[ids.numpy().astype(np.int64)], weight.dtype)
+
+
+def add_deepstack_rows(hidden_states, visual_token_rows, visual_embedding):
+    """``Qwen3VLLanguageModel._add_deepstack_rows``: ``nanovllm/models/qwen3_vl.py:332-344``.
+
+    Returns the input object itself when there are no rows; otherwise a new
+    tensor equal to the input except ``out[rows[j]] = h[rows[j]] + vis[j]``
+    (one activation-dtype rounding).
+    """
+    if visual_token_rows.numel() == 0:
+        return hidden_states
+    rows = visual_token_rows.long()
+    updated = hidden_states.index_select(0, rows) + visual_embedding
+    out = hidden_states.clone()
+    out.index_copy_(0, rows, updated)
+    return out
+
+
+# --------------------------------------------------------------------------- compositions
+
+
+def qk_norm_rope_store(
+    qkv,
+    num_heads,
+    num_kv_heads,
+    head_dim,
+    *,
+    positions,
+    rope,
+    q_weight=None,
+    k_weight=None,
+    eps=1e-6,
+    norm="rms",
+    key_cache=None,
+    value_cache=None,
+    slot_mapping=None,
+):
+    """The attention prologue that the fused kernel replaces.
+
+    Composition, per model:
+
+    * Qwen3 (``nanovllm/models/qwen3.py:77-86``): split ``qkv``, per-head
+      ``RMSNorm.rms_forward`` on q and k, 1-D ``RotaryEmbedding``, store.
+    * Qwen3-VL (``nanovllm/models/qwen3_vl.py:161-172``): per-head
+      ``Qwen3VLTextRMSNorm``, interleaved M-RoPE, store.
+    * Qwen2.5-VL (``nanovllm/models/qwen25_vl.py:66-76``): no q/k norm, chunked
+      M-RoPE, store.
+
+    ``rope`` is ``("table", cos_sin_cache)`` or
+    ``("mrope", inv_freq, sections, strategy)``; ``norm`` is ``"rms"``
+    (RMSNorm), ``"text"`` (Qwen3VLTextRMSNorm) or ``None``. The store writes
+    the rotated k and the raw v (``nanovllm/layers/attention.py:87-93``).
+    Returns ``(q, k, key_cache, value_cache)`` (caches are new tensors, or
+    ``None`` when not given).
+    """
+    q_size = num_heads * head_dim
+    kv_size = num_kv_heads * head_dim
+    q, k, v = qkv.split([q_size, kv_size, kv_size], dim=-1)
+    q = q.reshape(-1, num_heads, head_dim)
+    k = k.reshape(-1, num_kv_heads, head_dim)
+    v = v.reshape(-1, num_kv_heads, head_dim)
+    if norm == "rms":
+        q, k = rms_norm(q, q_weight, eps), rms_norm(k, k_weight, eps)
+    elif norm == "text":
+        q, k = text_rms_norm(q, q_weight, eps), text_rms_norm(k, k_weight, eps)
+    if rope[0] == "table":
+        q, k = apply_rope(positions, q, k, rope[1])
+    else:
+        _, inv_freq, sections, strategy = rope
+        q, k = mrope_forward(positions, q, k, inv_freq, sections, strategy)
+    kc = vc = None
+    if key_cache is not None:
+        kc, vc = paged_store(k, v, key_cache, value_cache, slot_mapping)
+    return q, k, kc, vc
+
+
+def qwen3_vl_fused_layer(
+    hidden,
+    residual,
+    qkv,
+    attn_out,
+    gate_up,
+    *,
+    positions,
+    inv_freq,
+    sections,
+    w_in,
+    w_post,
+    q_weight,
+    k_weight,
+    eps,
+    num_heads,
+    num_kv_heads,
+    head_dim,
+    key_cache,
+    value_cache,
+    slot_mapping,
+):
+    """One decoder layer's elementwise work with the GEMM outputs supplied.
+
+    ``nanovllm/models/qwen3_vl.py:226-240``: residual add + input norm, the
+    attention prologue (q/k norm, interleaved M-RoPE, paged store), residual add
+    + post-attention norm, and ``SiluAndMul`` on the gate/up projection. The
+    projections themselves (qkv, o_proj, gate_up) are inputs here.
+    Returns ``(normed_in, h1, q, k, key_cache, value_cache, normed_post, h2, act)``.
+    """
+    y1, h1 = add_text_rms_norm(hidden, residual, w_in, eps)
+    q, k, kc, vc = qk_norm_rope_store(
+        qkv, num_heads, num_kv_heads, head_dim,
+        positions=positions, rope=("mrope", inv_freq, sections, "interleaved"),
+        q_weight=q_weight, k_weight=k_weight, eps=eps, norm="text",
+        key_cache=key_cache, value_cache=value_cache, slot_mapping=slot_mapping,
+    )
+    y2, h2 = add_text_rms_norm(attn_out, h1, w_post, eps)
+    act = silu_and_mul(gate_up)
+    return y1, h1, q, k, kc, vc, y2, h2, act
