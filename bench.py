@@ -1,0 +1,568 @@
+#!/usr/bin/env python
+"""Benchmark of the per-token decoder elementwise path (NanoInfer hot path).
+
+Workload: config C5 (Qwen3-VL-2B shapes: hidden 2048, 16 q / 8 kv heads of
+128, intermediate 6144, interleaved M-RoPE [24,20,20] theta 5e6, q/k text
+norm). One STEP = 262,144 tokens through 28 fused layers plus the paged-KV
+gather of 64 sequences x 16,384 tokens (K and V caches). The tokens and
+sequences are split evenly over the ranks (strong scaling: total work per
+step is fixed); every rank owns its own 16,384 x 256-slot K/V cache pair and
+there is no collective on the data path.
+
+A fused layer = residual add + input text norm, the attention prologue (q/k
+norm + M-RoPE + paged store), residual add + post-attention norm, and
+SiluAndMul. The projections that feed it (qkv, o_proj, gate_up, down_proj)
+are out of scope: their outputs are fixed synthetic device tensors.
+
+``value``  = token x layer passes per second with inputs resident in HBM
+             (CUDA events on the launch stream, max over ranks).
+``e2e``    = the same through the layer-module API with the step's host inputs
+             (initial hidden states, positions, slot mapping) copied from
+             pinned memory and the final hidden states copied back each step.
+``--impl reference`` times the reference's CPU path (the oracle port of its
+PyTorch code) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+TOKENS = 262144
+LAYERS = 28
+GATHER_SEQS = 64
+GATHER_LEN = 16384
+CACHE_BLOCKS = 16384
+H, NQ, NKV, D, INTER = 2048, 16, 8, 128, 6144
+SECTIONS = (24, 20, 20)
+THETA = 5e6
+EPS = 1e-6
+METRIC = "fused-layer tokens/s"
+UNIT = "tokens/s"
+
+# algorithmic bytes per token (bf16) of each kernel of the fused layer
+BYTES = {
+    "add_rms_norm": 8 * H,                                                    # x, res in; y, res out
+    "qk_prologue": 2 * ((NQ + 2 * NKV) * D + NQ * D + NKV * D + 2 * NKV * D) + 8 * 3 + 4,
+    "silu_and_mul": 6 * INTER,                                                # gate, up in; out
+    "paged_gather": 2 * 2 * NKV * D,                                          # cache row in, out row
+}
+LAYER_BYTES = 2 * BYTES["add_rms_norm"] + BYTES["qk_prologue"] + BYTES["silu_and_mul"]
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--tokens", type=int, default=TOKENS, help="tokens per step (whole job)")
+    p.add_argument("--layers", type=int, default=LAYERS)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    return p.parse_args(argv)
+
+
+# ------------------------------------------------------------------ distributed plumbing
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def shard(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous even split of ``n`` units: rank r gets [start, start + count)."""
+    base, extra = divmod(n, world)
+    start = rank * base + min(rank, extra)
+    return start, base + (1 if rank < extra else 0)
+
+
+def max_over_ranks(value: float, world: int, device=None) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ clocks
+
+
+def physical_gpu(local: int) -> str:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if local < len(ids):
+            return ids[local]
+    return str(local)
+
+
+class ClockSampler:
+    """Samples ``nvidia-smi`` SM clocks / throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        return summarize_clocks(self.lines)
+
+
+def summarize_clocks(lines: list[str]) -> dict | None:
+    sm, smax, reasons = [], [], set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in lines:
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 9:
+            continue
+        try:
+            sm.append(float(f[1]))
+            smax.append(float(f[2]))
+        except ValueError:
+            continue
+        for name, flag in zip(names, f[5:9]):
+            if flag.lower() == "active":
+                reasons.add(name)
+    if not sm:
+        return None
+    top = max(sm)
+    loaded = [s for s in sm if s >= 0.5 * top] or sm
+    return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax) if smax else None,
+            "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ GPU workload
+
+
+def make_rank_inputs(rank: int, world: int, tokens_total: int, device):
+    from nano_vllm_multimodal_b200 import workloads as W
+
+    t0, T = shard(tokens_total, rank, world)
+    s0, S = shard(GATHER_SEQS, rank, world)
+    seeds = W._Seeds(5, device)
+    seeds.index = 100 * (rank + 1)
+    n = lambda shape, mean=0.0, std=1.0: W._normal(seeds, shape, mean, std)  # noqa: E731
+    inp = {
+        "tokens": T,
+        "hidden": n((T, H)), "residual": n((T, H)), "qkv": n((T, (NQ + 2 * NKV) * D)),
+        "attn_out": n((T, H)), "gate_up": n((T, 2 * INTER)), "mlp_out": n((T, H)),
+        "w_in": n((H,), 1.0, 0.1), "w_post": n((H,), 1.0, 0.1),
+        "q_weight": n((D,), 1.0, 0.1), "k_weight": n((D,), 1.0, 0.1),
+        "positions": torch.randint(0, 32768, (3, T), generator=seeds(), device=device),
+        "slot_mapping": torch.randperm(CACHE_BLOCKS * 256, generator=seeds(), device=device)[:T].to(torch.int32),
+        "inv_freq": (1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).to(device),
+    }
+    cache_shape = (CACHE_BLOCKS, 256, NKV, D)
+    inp["key_cache"] = torch.full(cache_shape, -3.0, dtype=torch.bfloat16, device=device)
+    inp["value_cache"] = torch.full(cache_shape, -3.0, dtype=torch.bfloat16, device=device)
+    need = GATHER_LEN // 256
+    inp["tables"] = torch.stack([torch.randperm(CACHE_BLOCKS, generator=seeds(), device=device)[:need]
+                                 for _ in range(S)]).to(torch.int32) if S else \
+        torch.empty(0, need, dtype=torch.int32, device=device)
+    inp["seq_lens"] = torch.full((S,), GATHER_LEN, dtype=torch.int32, device=device)
+    inp["cu_seqlens"] = torch.arange(S + 1, dtype=torch.int64, device=device) * GATHER_LEN
+    inp["gather_seqs"] = S
+    return inp
+
+
+class LaunchTimer:
+    """CUDA events around every launch on the current stream, per kernel name."""
+
+    def __init__(self):
+        self.pairs: dict[str, list] = {}
+
+    def __call__(self, name, fn, *a, **k):
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = fn(*a, **k)
+        e.record()
+        self.pairs.setdefault(name, []).append((s, e))
+        return out
+
+    def summary(self) -> dict[str, dict]:
+        out = {}
+        for name, pairs in self.pairs.items():
+            ms = [s.elapsed_time(e) for s, e in pairs]
+            out[name] = {"launches": len(ms), "total_ms": sum(ms), "avg_ms": sum(ms) / len(ms)}
+        return out
+
+
+def run_step(inp, layers, timer=None):
+    from nano_vllm_multimodal_b200 import ops
+
+    call = timer if timer is not None else (lambda name, fn, *a, **k: fn(*a, **k))
+    h, res = inp["hidden"], inp["residual"]
+    qkv = inp["qkv"]
+    q, k, v = qkv.split([NQ * D, NKV * D, NKV * D], -1)
+    q, k, v = q.view(-1, NQ, D), k.view(-1, NKV, D), v.view(-1, NKV, D)
+    h2 = None
+    for _ in range(layers):
+        _, h1 = call("add_rms_norm", ops.add_rms_norm, h, res, inp["w_in"], EPS, True)
+        call("qk_prologue", ops.qk_prologue, q, k, v=v, positions=inp["positions"],
+             q_weight=inp["q_weight"], k_weight=inp["k_weight"], eps=EPS,
+             rope_mode=ops.ROPE_MROPE_INTERLEAVED, inv_freq=inp["inv_freq"], sections=SECTIONS,
+             key_cache=inp["key_cache"], value_cache=inp["value_cache"],
+             slot_mapping=inp["slot_mapping"])
+        _, h2 = call("add_rms_norm", ops.add_rms_norm, inp["attn_out"], h1, inp["w_post"], EPS, True)
+        call("silu_and_mul", ops.silu_and_mul, inp["gate_up"])
+        h, res = inp["mlp_out"], h2
+    if inp["gather_seqs"]:
+        total = inp["gather_seqs"] * GATHER_LEN
+        for cache in (inp["key_cache"], inp["value_cache"]):
+            call("paged_gather", ops.paged_gather_varlen, cache, inp["tables"], inp["seq_lens"],
+                 inp["cu_seqlens"], total, GATHER_LEN)
+    return h2
+
+
+def launches_per_step(layers, gather_seqs):
+    return 4 * layers + (2 if gather_seqs else 0)
+
+
+def run_step_e2e(inp, layers, mods, host, dev_in):
+    """One step through the layer-module API, host buffers in and out."""
+    from nano_vllm_multimodal_b200.layers.attention import attention_prologue
+
+    dev_in["hidden"].copy_(host["hidden"], non_blocking=True)
+    dev_in["positions"].copy_(host["positions"], non_blocking=True)
+    dev_in["slot_mapping"].copy_(host["slot_mapping"], non_blocking=True)
+    h, res = dev_in["hidden"], inp["residual"]
+    h2 = None
+    for _ in range(layers):
+        _, h1 = mods["input_norm"](h, res)
+        attention_prologue(inp["qkv"], num_heads=NQ, num_kv_heads=NKV, head_dim=D,
+                           positions=dev_in["positions"], rotary_emb=mods["rope"], q_norm=mods["q_norm"],
+                           k_norm=mods["k_norm"], k_cache=inp["key_cache"], v_cache=inp["value_cache"],
+                           slot_mapping=dev_in["slot_mapping"])
+        _, h2 = mods["post_norm"](inp["attn_out"], h1)
+        mods["act"](inp["gate_up"])
+        h, res = inp["mlp_out"], h2
+    host["out"].copy_(h2, non_blocking=True)
+
+
+def build_modules(inp, device):
+    from nano_vllm_multimodal_b200.layers.activation import SiluAndMul
+    from nano_vllm_multimodal_b200.layers.multimodal_rotary_embedding import MultimodalRotaryEmbedding
+    from nano_vllm_multimodal_b200.layers.qwen3_vl import Qwen3VLTextRMSNorm
+
+    def norm(n, w):
+        m = Qwen3VLTextRMSNorm(n, eps=EPS).to(device=device, dtype=torch.bfloat16)
+        with torch.no_grad():
+            m.weight.copy_(w)
+        return m
+
+    rope = MultimodalRotaryEmbedding(head_dim=D, base=THETA, sections=SECTIONS, strategy="interleaved").to(device)
+    return {"input_norm": norm(H, inp["w_in"]), "post_norm": norm(H, inp["w_post"]),
+            "q_norm": norm(D, inp["q_weight"]), "k_norm": norm(D, inp["k_weight"]),
+            "rope": rope, "act": SiluAndMul()}
+
+
+def load_traffic_table() -> dict[str, float]:
+    """DRAM bytes per token per kernel from the committed ncu summary, if any."""
+    path = ROOT / "profiles" / "dram_traffic.md"
+    out = {}
+    if not path.exists():
+        return out
+    for m in re.finditer(r"^\|\s*(\w+)\s*\|\s*([0-9.]+)\s*\|", path.read_text(), re.M):
+        try:
+            out[m.group(1)] = float(m.group(2))
+        except ValueError:
+            pass
+    return out
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle port)
+
+
+def cpu_layer_sample(tokens: int, seed: int = 0):
+    """CPU inputs of one C5 fused layer over ``tokens`` tokens (256-block cache)."""
+    from nano_vllm_multimodal_b200 import workloads as W
+
+    seeds = W._Seeds(5, "cpu")
+    seeds.index = 900 + seed
+    n = lambda shape, mean=0.0, std=1.0: W._normal(seeds, shape, mean, std)  # noqa: E731
+    return {
+        "hidden": n((tokens, H)), "residual": n((tokens, H)), "qkv": n((tokens, (NQ + 2 * NKV) * D)),
+        "attn_out": n((tokens, H)), "gate_up": n((tokens, 2 * INTER)),
+        "w_in": n((H,), 1.0, 0.1), "w_post": n((H,), 1.0, 0.1),
+        "q_weight": n((D,), 1.0, 0.1), "k_weight": n((D,), 1.0, 0.1),
+        "positions": torch.randint(0, 32768, (3, tokens), generator=seeds()),
+        "slot_mapping": torch.randperm(256 * 256, generator=seeds())[:tokens].to(torch.int32),
+        "key_cache": torch.full((256, 256, NKV, D), -3.0, dtype=torch.bfloat16),
+        "value_cache": torch.full((256, 256, NKV, D), -3.0, dtype=torch.bfloat16),
+    }
+
+
+def cpu_layer(sample):
+    import oracle as O
+
+    O.qwen3_vl_fused_layer(
+        sample["hidden"], sample["residual"], sample["qkv"], sample["attn_out"], sample["gate_up"],
+        positions=sample["positions"], inv_freq=O.mrope_inv_freq(D, THETA), sections=SECTIONS,
+        w_in=sample["w_in"], w_post=sample["w_post"], q_weight=sample["q_weight"],
+        k_weight=sample["k_weight"], eps=EPS, num_heads=NQ, num_kv_heads=NKV, head_dim=D,
+        key_cache=sample["key_cache"], value_cache=sample["value_cache"],
+        slot_mapping=sample["slot_mapping"], inplace=True)
+
+
+def host_threads() -> int:
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return n
+
+
+def cpu_baseline(budget_s: float, tokens: int = 2048) -> dict:
+    cores = host_threads()
+    sample = cpu_layer_sample(tokens)
+    cpu_layer(sample)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        cpu_layer(sample)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 200:
+            break
+    return {"value": tokens * reps / el, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{reps} x one fused layer over {tokens} C5 tokens on the CPU oracle "
+                      f"(reference eager PyTorch ops), {el:.1f} s"}
+
+
+def config_block(args, world, extra=None):
+    cfg = {"workload": "C5 Qwen3-VL-2B fused elementwise layer x28 + paged-KV gather",
+           "tokens_per_step": args.tokens, "layers": args.layers, "hidden": H,
+           "heads": [NQ, NKV], "head_dim": D, "intermediate": INTER,
+           "mrope": {"strategy": "interleaved", "sections": list(SECTIONS), "theta": THETA},
+           "gather": {"sequences": GATHER_SEQS, "tokens_per_sequence": GATHER_LEN, "caches": 2},
+           "cache_per_gpu": [CACHE_BLOCKS, 256, NKV, D], "parallelism": f"token-sharded x{world}",
+           "value_counts": "token x fused-layer passes per second",
+           "l2": "inputs larger than L2 (every kernel's working set > 126 MB at every N)"}
+    if extra:
+        cfg.update(extra)
+    return cfg
+
+
+# ------------------------------------------------------------------ arms
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    cores = host_threads()
+    tokens = 4096
+    sample = cpu_layer_sample(tokens)
+    for _ in range(args.warmup):
+        cpu_layer(sample)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cpu_layer(sample)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = tokens * args.steps / total
+    desc = f"one C5 fused layer over {tokens} tokens per step on {cores} host threads (oracle port)"
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, C5 shapes)", "config": config_block(args, 1),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def ours_arm(args, rank, world, local):
+    from nano_vllm_multimodal_b200 import ops  # noqa: F401  (loads the extension, fails loudly)
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    inp = make_rank_inputs(rank, world, args.tokens, device)
+    T = inp["tokens"]
+    torch.cuda.synchronize()
+
+    # ---- warm-up + timed region (device-resident inputs)
+    for _ in range(args.warmup):
+        run_step(inp, args.layers)
+    torch.cuda.synchronize()
+    timer = LaunchTimer()
+    clocks = ClockSampler(physical_gpu(local))
+    if rank == 0:
+        clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        run_step(inp, args.layers, timer)
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clock = clocks.stop()
+    ms = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms, world, device)
+    kernels = timer.summary()
+
+    tokens_job = args.tokens
+    value = tokens_job * args.layers * args.steps / (ms_max / 1000.0)
+    gather_tokens = inp["gather_seqs"] * GATHER_LEN
+    step_bytes = T * args.layers * LAYER_BYTES + 2 * gather_tokens * BYTES["paged_gather"]
+    step_bytes_job = max_over_ranks(float(step_bytes), world, device) * world
+
+    # ---- per-kernel roofline (this rank's launches)
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    hbm_peak = peaks.get("hbm_gbs")
+    peak_src = "measured" if hbm_peak else "fallback"
+    hbm_peak = hbm_peak or 6650.0
+    traffic_tbl = load_traffic_table()
+    per_kernel = {}
+    for name, s in kernels.items():
+        units = gather_tokens if name == "paged_gather" else T
+        algo = BYTES[name] * units
+        gbs = algo / (s["avg_ms"] / 1000.0) / 1e9
+        per_kernel[name] = {"launches": s["launches"], "avg_ms": round(s["avg_ms"], 4),
+                            "share": None, "bytes_per_launch": algo, "achieved_gbs": round(gbs, 1),
+                            "frac": round(gbs / hbm_peak, 4)}
+    total_k = sum(s["total_ms"] for s in kernels.values())
+    for name, s in kernels.items():
+        per_kernel[name]["share"] = round(s["total_ms"] / total_k, 4)
+    dom = max(kernels, key=lambda n: kernels[n]["total_ms"])
+    traffic = None
+    if dom in traffic_tbl:
+        traffic = traffic_tbl[dom] * (gather_tokens if dom == "paged_gather" else T)
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": per_kernel[dom]["achieved_gbs"],
+                "peak": hbm_peak, "unit": "GB/s", "frac": per_kernel[dom]["frac"], "traffic": traffic,
+                "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)"}
+
+    # ---- e2e through the layer API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        mods = build_modules(inp, device)
+        host = {"hidden": inp["hidden"].cpu().pin_memory(), "positions": inp["positions"].cpu().pin_memory(),
+                "slot_mapping": inp["slot_mapping"].cpu().pin_memory(),
+                "out": torch.empty(T, H, dtype=torch.bfloat16).pin_memory()}
+        dev_in = {"hidden": torch.empty_like(inp["hidden"]), "positions": torch.empty_like(inp["positions"]),
+                  "slot_mapping": torch.empty_like(inp["slot_mapping"])}
+        for _ in range(max(1, args.warmup)):
+            run_step_e2e(inp, args.layers, mods, host, dev_in)
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            run_step_e2e(inp, args.layers, mods, host, dev_in)
+        e.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        e_ms = max_over_ranks(s.elapsed_time(e), world, device)
+        h2d = sum(host[k].numel() * host[k].element_size() for k in ("hidden", "positions", "slot_mapping"))
+        d2h = host["out"].numel() * host["out"].element_size()
+        e2e = {"value": tokens_job * args.layers * args.steps / (e_ms / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": int(max_over_ranks(float(h2d), world, device) * world),
+               "d2h_bytes_per_step": int(max_over_ranks(float(d2h), world, device) * world),
+               "ms_per_step": e_ms / args.steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, C5 shapes, random-init norm weights)",
+        "config": config_block(args, world),
+        "hbm": {"algorithmic_bytes_per_step": step_bytes_job,
+                "gbs": step_bytes_job / (ms_max / args.steps / 1000.0) / 1e9,
+                "frac_of_peak": step_bytes_job / (ms_max / args.steps / 1000.0) / 1e9 / hbm_peak,
+                "peak_gbs": hbm_peak},
+        "roofline": roofline, "kernels": per_kernel,
+        "e2e": e2e, "cpu_baseline": cpu, "clocks": clock,
+        "gpu_launches": launches_per_step(args.layers, inp["gather_seqs"]) * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    if world != args.gpus and world == 1 and args.gpus > 1:
+        print(f"bench.py: --gpus {args.gpus} needs torchrun with {args.gpus} processes", file=sys.stderr)
+        return 2
+    return ours_arm(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

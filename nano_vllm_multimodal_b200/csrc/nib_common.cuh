@@ -1,0 +1,159 @@
+// Shared device helpers for the sm_100a elementwise kernels.
+//
+// All HBM traffic goes through 16-byte vectors (one LDG.128 / STG.128 per
+// lane); element conversions are explicit so the rounding points match the
+// reference's PyTorch code exactly (fp32 math, round-to-nearest-even to the
+// storage dtype where PyTorch rounds).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/nib_b200.h"
+
+namespace nib {
+
+// ---------------------------------------------------------------- host side
+void set_error(const char* fmt, ...);
+int launch_status(const char* what);  // NIB_OK or NIB_ERR_CUDA after a launch
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// number of SMs of the current device (cached per device)
+int sm_count();
+
+#define NIB_REQUIRE(cond, ...)                 \
+  do {                                         \
+    if (!(cond)) {                             \
+      ::nib::set_error(__VA_ARGS__);           \
+      return NIB_ERR_INVALID;                  \
+    }                                          \
+  } while (0)
+
+#define NIB_SUPPORT(cond, ...)                 \
+  do {                                         \
+    if (!(cond)) {                             \
+      ::nib::set_error(__VA_ARGS__);           \
+      return NIB_ERR_UNSUPPORTED;              \
+    }                                          \
+  } while (0)
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int elem_size(int dtype) { return dtype == NIB_F32 ? 4 : 2; }
+
+// ---------------------------------------------------------------- element traits
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static constexpr int kPerVec = 4;
+  __device__ __forceinline__ static float to_f(float v) { return v; }
+  __device__ __forceinline__ static float from_f(float v) { return v; }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr int kPerVec = 8;
+  __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+template <> struct Elem<__half> {
+  static constexpr int kPerVec = 8;
+  __device__ __forceinline__ static float to_f(__half v) { return __half2float(v); }
+  __device__ __forceinline__ static __half from_f(float v) { return __float2half_rn(v); }
+};
+
+// round an fp32 value to T and back (identity for float)
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  return Elem<T>::to_f(Elem<T>::from_f(v));
+}
+
+// ---------------------------------------------------------------- 16-byte vectors
+__device__ __forceinline__ uint4 ld_vec(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+// read-once streaming input: evict-first in L1/L2
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void st_vec(void* p, const uint4& v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
+__device__ __forceinline__ uint4 zero_vec() { return make_uint4(0u, 0u, 0u, 0u); }
+
+// unpack one 16-byte vector of T into kPerVec floats
+template <typename T>
+__device__ __forceinline__ void unpack(const uint4& v, float* f);
+
+template <>
+__device__ __forceinline__ void unpack<float>(const uint4& v, float* f) {
+  f[0] = __uint_as_float(v.x); f[1] = __uint_as_float(v.y);
+  f[2] = __uint_as_float(v.z); f[3] = __uint_as_float(v.w);
+}
+template <>
+__device__ __forceinline__ void unpack<__nv_bfloat16>(const uint4& v, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+template <>
+__device__ __forceinline__ void unpack<__half>(const uint4& v, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+    float2 t = __half22float2(h);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// pack kPerVec floats into one 16-byte vector of T (round to nearest even)
+template <typename T>
+__device__ __forceinline__ uint4 pack(const float* f);
+
+template <>
+__device__ __forceinline__ uint4 pack<float>(const float* f) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                    __float_as_uint(f[3]));
+}
+template <>
+__device__ __forceinline__ uint4 pack<__nv_bfloat16>(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <>
+__device__ __forceinline__ uint4 pack<__half>(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// load kPerVec<T> weights starting at element i as floats (W = T or float)
+template <typename T, typename W>
+__device__ __forceinline__ void load_weights(const W* w, int64_t i, float* f) {
+  constexpr int E = Elem<T>::kPerVec;
+  if constexpr (sizeof(W) == sizeof(T)) {
+    unpack<T>(ld_vec(w + i), f);
+  } else {
+    // fp32 weights with 16-bit activations: two 16-byte loads
+#pragma unroll
+    for (int j = 0; j < E; j += 4) unpack<float>(ld_vec(w + i + j), f + j);
+  }
+}
+
+__device__ __forceinline__ void flag(unsigned int* status, unsigned int bit) {
+  if (status != nullptr) atomicOr(status, bit);
+}
+
+}  // namespace nib

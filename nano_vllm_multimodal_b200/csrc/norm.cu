@@ -1,0 +1,271 @@
+// RMSNorm and fused residual-add + RMSNorm (HBM-bound row kernels).
+//
+// Reference numerics (nanovllm/layers/layernorm.py:16-40,
+// nanovllm/models/qwen3_vl.py:74-79,232-237):
+//   s   = x (+ residual)            fp32 add; Qwen3-VL rounds s to the dtype first
+//   var = mean(s^2)                 fp32
+//   n   = dtype(s * (1/sqrt(var + eps)))
+//   y   = dtype(n * w)              one more rounding
+// The 1/sqrt is the IEEE sqrt followed by the IEEE divide (what PyTorch's CPU
+// rsqrt computes); squares are rounded before they are summed, as
+// `x.pow(2).mean()` does. Only the summation order differs from PyTorch.
+//
+// Layout: rows of n elements, each row read once with 16-byte vectors and
+// written once. Rows of up to 256 vectors (2048 bf16) live in one warp's
+// registers (G lanes x VPT vectors); longer rows use one CTA per row.
+#include "dispatch.cuh"
+
+namespace nib {
+
+template <typename T, typename W, int G, int VPT>
+__global__ void __launch_bounds__(256)
+rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __restrict__ res,
+              int64_t r_rs, const W* __restrict__ w, T* __restrict__ y, T* __restrict__ res_out,
+              int64_t rows, int64_t heads, int n, float eps, int add, int round_sum) {
+  constexpr int E = Elem<T>::kPerVec;
+  constexpr int GPW = 32 / G;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane / G;
+  const int gl = lane % G;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int nv = n / E;
+  for (int64_t rb = warp * GPW; rb < rows; rb += nwarps * GPW) {
+    const int64_t r = rb + sub;
+    const bool active = r < rows;
+    int64_t t = 0, h = 0;
+    if (active) {
+      t = heads == 1 ? r : r / heads;
+      h = r - t * heads;
+    }
+    const T* xp = x + t * x_ts + h * x_hs;
+    const T* rp = add ? res + t * r_rs : nullptr;
+    uint4 xr[VPT], rr[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = i * G + gl;
+      const bool ok = active && vi < nv;
+      xr[i] = ok ? ld_stream(xp + vi * E) : zero_vec();
+      rr[i] = (ok && add) ? ld_stream(rp + vi * E) : zero_vec();
+    }
+    float v[VPT][E];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      unpack<T>(xr[i], v[i]);
+      if (add) {
+        float rv[E];
+        unpack<T>(rr[i], rv);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float s = __fadd_rn(v[i][e], rv[e]);
+          v[i][e] = round_sum ? round_to<T>(s) : s;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) ss = __fadd_rn(ss, __fmul_rn(v[i][e], v[i][e]));
+    }
+#pragma unroll
+    for (int off = G / 2; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+    const float rs = 1.0f / sqrtf(__fadd_rn(ss / static_cast<float>(n), eps));
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = i * G + gl;
+      if (!(active && vi < nv)) continue;
+      if (add) st_vec(res_out + r * n + vi * E, pack<T>(v[i]));
+      float wf[E];
+      load_weights<T, W>(w, vi * E, wf);
+      float o[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) o[e] = __fmul_rn(round_to<T>(__fmul_rn(v[i][e], rs)), wf[e]);
+      st_vec(y + r * n + vi * E, pack<T>(o));
+    }
+  }
+}
+
+// One CTA per row (rows longer than 256 vectors); VPT vectors per thread.
+template <typename T, typename W, int VPT>
+__global__ void __launch_bounds__(1024)
+rms_rows_block(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __restrict__ res,
+               int64_t r_rs, const W* __restrict__ w, T* __restrict__ y, T* __restrict__ res_out,
+               int64_t rows, int64_t heads, int n, float eps, int add, int round_sum) {
+  constexpr int E = Elem<T>::kPerVec;
+  __shared__ float red[32];
+  const int nv = n / E;
+  const int nwarp = blockDim.x >> 5;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int64_t t = heads == 1 ? r : r / heads;
+    const int64_t h = r - t * heads;
+    const T* xp = x + t * x_ts + h * x_hs;
+    const T* rp = add ? res + t * r_rs : nullptr;
+    uint4 xr[VPT], rr[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = i * blockDim.x + threadIdx.x;
+      const bool ok = vi < nv;
+      xr[i] = ok ? ld_stream(xp + vi * E) : zero_vec();
+      rr[i] = (ok && add) ? ld_stream(rp + vi * E) : zero_vec();
+    }
+    float v[VPT][E];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      unpack<T>(xr[i], v[i]);
+      if (add) {
+        float rv[E];
+        unpack<T>(rr[i], rv);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float s = __fadd_rn(v[i][e], rv[e]);
+          v[i][e] = round_sum ? round_to<T>(s) : s;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) ss = __fadd_rn(ss, __fmul_rn(v[i][e], v[i][e]));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < nwarp; ++i) tot = __fadd_rn(tot, red[i]);
+    __syncthreads();  // red is rewritten by the next row
+    const float rs = 1.0f / sqrtf(__fadd_rn(tot / static_cast<float>(n), eps));
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = i * blockDim.x + threadIdx.x;
+      if (vi >= nv) continue;
+      if (add) st_vec(res_out + r * n + vi * E, pack<T>(v[i]));
+      float wf[E];
+      load_weights<T, W>(w, vi * E, wf);
+      float o[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) o[e] = __fmul_rn(round_to<T>(__fmul_rn(v[i][e], rs)), wf[e]);
+      st_vec(y + r * n + vi * E, pack<T>(o));
+    }
+  }
+}
+
+template <typename T, typename W, int G, int VPT>
+static void launch_warp(const void* x, int64_t x_ts, int64_t x_hs, const void* res, int64_t r_rs,
+                        const void* w, void* y, void* res_out, int64_t rows, int64_t heads, int n,
+                        float eps, int add, int round_sum, cudaStream_t st) {
+  constexpr int kThreads = 256;
+  constexpr int rows_per_block = (kThreads / 32) * (32 / G);
+  int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 32;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  rms_rows_warp<T, W, G, VPT><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+      static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
+      static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
+      add, round_sum);
+}
+
+template <typename T, typename W>
+static int launch_rms(const void* x, int64_t x_ts, int64_t x_hs, const void* res, int64_t r_rs,
+                      const void* w, void* y, void* res_out, int64_t rows, int64_t heads,
+                      int64_t n64, float eps, int add, int round_sum, cudaStream_t st) {
+  constexpr int E = Elem<T>::kPerVec;
+  const int n = static_cast<int>(n64);
+  const int nv = n / E;
+  if (nv <= 16 && !add) {
+    if (nv <= 1) launch_warp<T, W, 1, 1>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (nv <= 2) launch_warp<T, W, 2, 1>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (nv <= 4) launch_warp<T, W, 4, 1>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (nv <= 8) launch_warp<T, W, 8, 1>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else launch_warp<T, W, 16, 1>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    return launch_status("rms_norm");
+  }
+  if (nv <= 256) {
+    const int vpt = (nv + 31) / 32;
+    switch (vpt) {
+#define NIB_RMS_VPT(V) \
+      case V: launch_warp<T, W, 32, V>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st); break;
+      NIB_RMS_VPT(1) NIB_RMS_VPT(2) NIB_RMS_VPT(3) NIB_RMS_VPT(4)
+      NIB_RMS_VPT(5) NIB_RMS_VPT(6) NIB_RMS_VPT(7) NIB_RMS_VPT(8)
+#undef NIB_RMS_VPT
+    }
+    return launch_status("rms_norm");
+  }
+  // long rows: one CTA per row, 4 vectors per thread
+  int threads = ((nv + 3) / 4 + 31) / 32 * 32;
+  NIB_SUPPORT(threads <= 1024, "rms_norm: row of %d elements is longer than this build supports", n);
+  int64_t blocks = rows;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / threads);
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  rms_rows_block<T, W, 4><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+      static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
+      static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
+      add, round_sum);
+  return launch_status("rms_norm");
+}
+
+template <typename T>
+static int dispatch_weight(int weight_dtype, int dtype, const void* x, int64_t x_ts, int64_t x_hs,
+                           const void* res, int64_t r_rs, const void* w, void* y, void* res_out,
+                           int64_t rows, int64_t heads, int64_t n, float eps, int add,
+                           int round_sum, cudaStream_t st) {
+  if (weight_dtype == dtype)
+    return launch_rms<T, T>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+  if (weight_dtype == NIB_F32)
+    return launch_rms<T, float>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+  set_error("rms_norm: weight dtype %d must equal the activation dtype %d or be float32", weight_dtype, dtype);
+  return NIB_ERR_UNSUPPORTED;
+}
+
+static int check_vec_rows(int dtype, const void* p, int64_t s1, int64_t s2, int64_t n, const char* what) {
+  const int E = 16 / elem_size(dtype);
+  NIB_SUPPORT(aligned16(p), "%s: data pointer is not 16-byte aligned", what);
+  NIB_SUPPORT(n % E == 0, "%s: row length %lld is not a multiple of %d elements", what, (long long)n, E);
+  NIB_SUPPORT(s1 % E == 0 && s2 % E == 0, "%s: strides must be multiples of %d elements", what, E);
+  return NIB_OK;
+}
+
+}  // namespace nib
+
+using namespace nib;
+
+extern "C" int nib_rms_norm(int dtype, const void* x, int64_t x_token_stride, int64_t x_head_stride,
+                            int64_t tokens, int64_t heads, int64_t n, int weight_dtype,
+                            const void* weight, float eps, void* out, void* stream) {
+  NIB_REQUIRE(tokens >= 0 && heads >= 1 && n >= 1, "rms_norm: bad sizes");
+  if (tokens == 0) return NIB_OK;
+  NIB_REQUIRE(x && weight && out, "rms_norm: null pointer");
+  int rc = check_vec_rows(dtype, x, x_token_stride, x_head_stride, n, "rms_norm input");
+  if (rc) return rc;
+  rc = check_vec_rows(dtype, out, 0, 0, n, "rms_norm output");
+  if (rc) return rc;
+  NIB_SUPPORT(aligned16(weight), "rms_norm: weight is not 16-byte aligned");
+  NIB_SUPPORT(dtype != NIB_F32 || weight_dtype == NIB_F32, "rms_norm: float32 input needs float32 weight");
+  NIB_DISPATCH(dtype, T,
+               return dispatch_weight<T>(weight_dtype, dtype, x, x_token_stride, x_head_stride,
+                                         nullptr, 0, weight, out, nullptr, tokens * heads, heads, n,
+                                         eps, 0, 0, as_stream(stream)));
+  return NIB_OK;
+}
+
+extern "C" int nib_add_rms_norm(int dtype, const void* x, int64_t x_row_stride, const void* residual,
+                                int64_t residual_row_stride, int64_t rows, int64_t n,
+                                int weight_dtype, const void* weight, float eps, int round_sum,
+                                void* out, void* residual_out, void* stream) {
+  NIB_REQUIRE(rows >= 0 && n >= 1, "add_rms_norm: bad sizes");
+  if (rows == 0) return NIB_OK;
+  NIB_REQUIRE(x && residual && weight && out && residual_out, "add_rms_norm: null pointer");
+  int rc = check_vec_rows(dtype, x, x_row_stride, 0, n, "add_rms_norm input");
+  if (rc) return rc;
+  rc = check_vec_rows(dtype, residual, residual_row_stride, 0, n, "add_rms_norm residual");
+  if (rc) return rc;
+  rc = check_vec_rows(dtype, out, 0, 0, n, "add_rms_norm output");
+  if (rc) return rc;
+  rc = check_vec_rows(dtype, residual_out, 0, 0, n, "add_rms_norm residual output");
+  if (rc) return rc;
+  NIB_SUPPORT(aligned16(weight), "add_rms_norm: weight is not 16-byte aligned");
+  NIB_SUPPORT(dtype != NIB_F32 || weight_dtype == NIB_F32, "add_rms_norm: float32 input needs float32 weight");
+  NIB_DISPATCH(dtype, T,
+               return dispatch_weight<T>(weight_dtype, dtype, x, x_row_stride, 0, residual,
+                                         residual_row_stride, weight, out, residual_out, rows, 1, n,
+                                         eps, 1, round_sum ? 1 : 0, as_stream(stream)));
+  return NIB_OK;
+}

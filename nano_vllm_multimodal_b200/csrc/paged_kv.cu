@@ -1,0 +1,185 @@
+// Paged KV cache store / gather (byte-exact copies).
+//
+// store:  csrc/paged_kv/paged_kv_cuda.cu:21-59 semantics - token t with
+//         slot s = slot_mapping[t] >= 0 overwrites flat slot s of the key and
+//         value caches; s == -1 skips the token; other slots keep their bytes.
+// gather: csrc/paged_kv/paged_kv_cuda.cu:61-94 semantics -
+//         out[t] = cache[block_table[t / block_size], t % block_size].
+//
+// One warp per token row; rows move as 16-byte vectors whenever every
+// address and stride is 16-byte aligned (else 8/4/2). Out-of-range slots and
+// block ids are never dereferenced: they set a status bit (store skips the
+// token, gather writes a zero row).
+#include "copy_rows.cuh"
+#include "dispatch.cuh"
+
+namespace nib {
+
+template <int VW>
+__global__ void __launch_bounds__(256)
+paged_store_kernel(const char* __restrict__ key, int64_t kts, const char* __restrict__ value,
+                   int64_t vts, int64_t tokens, int units, char* __restrict__ kc,
+                   char* __restrict__ vc, int64_t css, int64_t num_slots,
+                   const int32_t* __restrict__ slots, unsigned int* status) {
+  using V = typename VecOf<VW>::type;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t t = warp; t < tokens; t += nwarps) {
+    const int32_t sv = __ldg(slots + t);
+    if (sv < 0 || sv >= num_slots) {
+      if (sv != -1 && lane == 0) flag(status, NIB_DEV_BAD_SLOT);
+      continue;
+    }
+    const V* ks = reinterpret_cast<const V*>(key + t * kts);
+    const V* vs = reinterpret_cast<const V*>(value + t * vts);
+    V* kd = reinterpret_cast<V*>(kc + static_cast<int64_t>(sv) * css);
+    V* vd = reinterpret_cast<V*>(vc + static_cast<int64_t>(sv) * css);
+    for (int base = 0; base < units; base += 128) {
+      V a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int u = base + i * 32 + lane;
+        if (u < units) {
+          a[i] = __ldg(ks + u);
+          b[i] = __ldg(vs + u);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int u = base + i * 32 + lane;
+        if (u < units) {
+          kd[u] = a[i];
+          vd[u] = b[i];
+        }
+      }
+    }
+  }
+}
+
+// blockIdx.y = sequence; warps of the x-grid stride over that sequence's tokens.
+template <int VW>
+__global__ void __launch_bounds__(256)
+paged_gather_kernel(const char* __restrict__ cache, int64_t bst, int64_t sst, int64_t nblocks,
+                    int64_t bs, int units, const int32_t* __restrict__ tables, int64_t table_stride,
+                    const int32_t* __restrict__ seq_lens, const int64_t* __restrict__ cu,
+                    int64_t fixed_len, char* __restrict__ out, int64_t row_bytes,
+                    unsigned int* status) {
+  const int lane = threadIdx.x & 31;
+  const int64_t seq = blockIdx.y;
+  const int64_t len = seq_lens ? static_cast<int64_t>(__ldg(seq_lens + seq)) : fixed_len;
+  const int64_t obase = cu ? __ldg(cu + seq) : 0;
+  const int32_t* tbl = tables + seq * table_stride;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t t = warp; t < len; t += nwarps) {
+    const int64_t lb = t / bs;
+    const int64_t off = t - lb * bs;
+    const int32_t b = __ldg(tbl + lb);
+    char* dst = out + (obase + t) * row_bytes;
+    if (b < 0 || b >= nblocks) {
+      if (lane == 0) flag(status, NIB_DEV_BAD_BLOCK);
+      warp_zero_row<VW>(dst, units, lane);
+      continue;
+    }
+    warp_copy_row<VW>(dst, cache + static_cast<int64_t>(b) * bst + off * sst, units, lane);
+  }
+}
+
+static unsigned grid_for_rows(int64_t rows, int warps_per_block, int per_sm) {
+  int64_t blocks = (rows + warps_per_block - 1) / warps_per_block;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<unsigned>(blocks);
+}
+
+static int gather_impl(int dtype, const void* cache, int64_t block_stride, int64_t slot_stride,
+                       int64_t num_blocks, int64_t block_size, int64_t row_elems,
+                       const int32_t* tables, int64_t table_stride, const int32_t* seq_lens,
+                       const int64_t* cu, int64_t num_seqs, int64_t max_len, void* out,
+                       unsigned int* status, cudaStream_t st) {
+  const int es = elem_size(dtype);
+  const int64_t row_bytes = row_elems * es;
+  const int vw = pick_vec_width({reinterpret_cast<uint64_t>(cache), reinterpret_cast<uint64_t>(out),
+                                 static_cast<uint64_t>(block_stride * es),
+                                 static_cast<uint64_t>(slot_stride * es),
+                                 static_cast<uint64_t>(row_bytes)});
+  const int units = static_cast<int>(row_bytes / vw);
+  NIB_SUPPORT(num_seqs <= 65535, "paged gather: at most 65535 sequences per launch");
+  dim3 grid(grid_for_rows(max_len, 8, 16), static_cast<unsigned>(num_seqs));
+  NIB_VW_SWITCH(vw, VW,
+                paged_gather_kernel<VW><<<grid, 256, 0, st>>>(
+                    static_cast<const char*>(cache), block_stride * es, slot_stride * es, num_blocks,
+                    block_size, units, tables, table_stride, seq_lens, cu, max_len,
+                    static_cast<char*>(out), row_bytes, status));
+  return launch_status("paged_gather");
+}
+
+}  // namespace nib
+
+using namespace nib;
+
+extern "C" int nib_paged_store(int dtype, const void* key, int64_t key_token_stride,
+                               const void* value, int64_t value_token_stride, int64_t tokens,
+                               int64_t row_elems, void* key_cache, void* value_cache,
+                               int64_t cache_slot_stride, int64_t num_slots,
+                               const int32_t* slot_mapping, unsigned int* status, void* stream) {
+  NIB_REQUIRE(tokens >= 0 && row_elems >= 1 && num_slots >= 0, "paged_store: bad sizes");
+  if (tokens == 0) return NIB_OK;
+  NIB_REQUIRE(key && value && key_cache && value_cache && slot_mapping, "paged_store: null pointer");
+  NIB_REQUIRE(dtype == NIB_F32 || dtype == NIB_F16 || dtype == NIB_BF16, "paged_store: bad dtype");
+  const int es = elem_size(dtype);
+  const int64_t row_bytes = row_elems * es;
+  const int vw = pick_vec_width({reinterpret_cast<uint64_t>(key), reinterpret_cast<uint64_t>(value),
+                                 reinterpret_cast<uint64_t>(key_cache),
+                                 reinterpret_cast<uint64_t>(value_cache),
+                                 static_cast<uint64_t>(key_token_stride * es),
+                                 static_cast<uint64_t>(value_token_stride * es),
+                                 static_cast<uint64_t>(cache_slot_stride * es),
+                                 static_cast<uint64_t>(row_bytes)});
+  const int units = static_cast<int>(row_bytes / vw);
+  const cudaStream_t st = as_stream(stream);
+  const unsigned grid = grid_for_rows(tokens, 8, 16);
+  NIB_VW_SWITCH(vw, VW,
+                paged_store_kernel<VW><<<grid, 256, 0, st>>>(
+                    static_cast<const char*>(key), key_token_stride * es,
+                    static_cast<const char*>(value), value_token_stride * es, tokens, units,
+                    static_cast<char*>(key_cache), static_cast<char*>(value_cache),
+                    cache_slot_stride * es, num_slots, slot_mapping, status));
+  return launch_status("paged_store");
+}
+
+extern "C" int nib_paged_gather(int dtype, const void* cache, int64_t block_stride,
+                                int64_t slot_stride, int64_t num_blocks, int64_t block_size,
+                                int64_t row_elems, const int32_t* block_table,
+                                int64_t sequence_length, void* out, unsigned int* status,
+                                void* stream) {
+  NIB_REQUIRE(sequence_length >= 0 && row_elems >= 1 && block_size >= 1 && num_blocks >= 0,
+              "paged_gather: bad sizes");
+  if (sequence_length == 0) return NIB_OK;
+  NIB_REQUIRE(cache && block_table && out, "paged_gather: null pointer");
+  NIB_REQUIRE(dtype == NIB_F32 || dtype == NIB_F16 || dtype == NIB_BF16, "paged_gather: bad dtype");
+  return gather_impl(dtype, cache, block_stride, slot_stride, num_blocks, block_size, row_elems,
+                     block_table, 0, nullptr, nullptr, 1, sequence_length, out, status,
+                     as_stream(stream));
+}
+
+extern "C" int nib_paged_gather_varlen(int dtype, const void* cache, int64_t block_stride,
+                                       int64_t slot_stride, int64_t num_blocks, int64_t block_size,
+                                       int64_t row_elems, const int32_t* block_tables,
+                                       int64_t table_stride, const int32_t* seq_lens,
+                                       const int64_t* cu_seqlens, int64_t num_seqs,
+                                       int64_t max_seq_len, void* out, unsigned int* status,
+                                       void* stream) {
+  NIB_REQUIRE(num_seqs >= 0 && max_seq_len >= 0 && row_elems >= 1 && block_size >= 1,
+              "paged_gather_varlen: bad sizes");
+  if (num_seqs == 0 || max_seq_len == 0) return NIB_OK;
+  NIB_REQUIRE(cache && block_tables && seq_lens && cu_seqlens && out,
+              "paged_gather_varlen: null pointer");
+  NIB_REQUIRE(dtype == NIB_F32 || dtype == NIB_F16 || dtype == NIB_BF16,
+              "paged_gather_varlen: bad dtype");
+  return gather_impl(dtype, cache, block_stride, slot_stride, num_blocks, block_size, row_elems,
+                     block_tables, table_stride, seq_lens, cu_seqlens, num_seqs, max_seq_len, out,
+                     status, as_stream(stream));
+}

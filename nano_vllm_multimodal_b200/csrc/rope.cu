@@ -1,0 +1,406 @@
+// Attention prologue: per-head q/k RMSNorm + RoPE / M-RoPE + paged KV store.
+//
+// Reference composition (each stage's numerics kept exactly):
+//   q_norm/k_norm   RMSNorm.rms_forward (nanovllm/layers/layernorm.py:16-26) or
+//                   Qwen3VLTextRMSNorm (nanovllm/models/qwen3_vl.py:74-79)
+//   1-D RoPE        nanovllm/layers/rotary_embedding.py:6-14,37-48 - fp32 math
+//                   on the fp32 cos|sin table, one rounding at the end
+//   M-RoPE          nanovllm/layers/multimodal_rotary_embedding.py:12-45,89-147
+//                   cos/sin = dtype(cos/sin(fp32(pos) * inv_freq));
+//                   chunked: fp32 math, one rounding;
+//                   interleaved: dtype arithmetic, every product and the sum
+//                   rounded (round(round(x*c) + round(rot(x)*s)))
+//   store           rotated k and raw v to flat slot slot_mapping[t]
+//                   (nanovllm/layers/attention.py:87-93), -1 skipped.
+//
+// Layout: a warp owns one token; each head is covered by LPH = head_dim / 8
+// lanes holding one 16-byte vector each (bf16/fp16), so a warp processes
+// 32 / LPH heads per step. The rotate-half partner of lane l is lane l ^ LPH/2
+// (one shuffle per 32-bit word). A work item is (token, chunk of up to 8 head
+// groups); all 8 loads of an item are issued before any math. M-RoPE cos/sin
+// are computed once per item for the head_dim/2 frequencies (each lane handles
+// head_dim/64 of them) and shared through shared memory.
+#include "dispatch.cuh"
+
+namespace nib {
+
+constexpr int kPrologueWarps = 4;
+constexpr int kChunk = 8;
+
+template <typename T, typename W, int D>
+__global__ void __launch_bounds__(kPrologueWarps * 32)
+qk_prologue_kernel(const nib_qk_prologue_args a) {
+  constexpr int E = Elem<T>::kPerVec;
+  constexpr int LPH = D / E;
+  static_assert(LPH >= 2 && LPH <= 32, "head must span 2..32 lanes");
+  constexpr int HPW = 32 / LPH;
+  constexpr int HALF = LPH / 2;
+  constexpr int NF = D / 2;
+  __shared__ float s_cos[kPrologueWarps][NF];
+  __shared__ float s_sin[kPrologueWarps][NF];
+
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  const int hs = lane / LPH;
+  const int l = lane % LPH;
+  const bool first = l < HALF;
+  const int fb = (l % HALF) * E;
+
+  const int nq = a.num_heads, nkv = a.num_kv_heads;
+  const int Uq = (nq + HPW - 1) / HPW;
+  const int Uk = (nkv + HPW - 1) / HPW;
+  const bool store = a.key_cache != nullptr;
+  const int Uv = store ? Uk : 0;
+  const int U = Uq + Uk + Uv;
+  const int nchunks = (U + kChunk - 1) / kChunk;
+  const int64_t items = a.tokens * nchunks;
+
+  const T* q = static_cast<const T*>(a.q);
+  const T* k = static_cast<const T*>(a.k);
+  const T* v = static_cast<const T*>(a.v);
+  T* q_out = static_cast<T*>(a.q_out);
+  T* k_out = static_cast<T*>(a.k_out);
+  T* kc = static_cast<T*>(a.key_cache);
+  T* vc = static_cast<T*>(a.value_cache);
+  const W* qw = static_cast<const W*>(a.q_weight);
+  const W* kw = static_cast<const W*>(a.k_weight);
+
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+
+  for (int64_t it = warp; it < items; it += nwarps) {
+    const int64_t t = it / nchunks;
+    const int chunk = static_cast<int>(it - t * nchunks);
+    const int u0 = chunk * kChunk;
+
+    int64_t slot = -1;
+    if (store) {
+      const int32_t sv = __ldg(a.slot_mapping + t);
+      if (sv >= 0 && sv < a.num_slots) {
+        slot = sv;
+      } else if (sv != -1 && chunk == 0 && lane == 0) {
+        flag(a.status, NIB_DEV_BAD_SLOT);
+      }
+    }
+
+    // ---- issue every load of this item first
+    uint4 buf[kChunk];
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) {
+      const int u = u0 + i;
+      buf[i] = zero_vec();
+      if (u < Uq) {
+        const int head = u * HPW + hs;
+        if (head < nq) buf[i] = ld_stream(q + t * a.q_token_stride + head * a.q_head_stride + l * E);
+      } else if (u < Uq + Uk) {
+        const int head = (u - Uq) * HPW + hs;
+        if (head < nkv) buf[i] = ld_stream(k + t * a.k_token_stride + head * a.k_head_stride + l * E);
+      } else if (u < U && slot >= 0) {
+        const int head = (u - Uq - Uk) * HPW + hs;
+        if (head < nkv) buf[i] = ld_stream(v + t * a.v_token_stride + head * a.v_head_stride + l * E);
+      }
+    }
+
+    // ---- cos / sin of this lane's E frequencies (only if the item rotates something)
+    float c[E], s[E];
+    const bool rotates = a.rope_mode != NIB_ROPE_NONE && u0 < Uq + Uk;
+    if (rotates) {
+      if (a.rope_mode == NIB_ROPE_TABLE) {
+        const int64_t p = __ldg(a.positions + t * a.positions_token_stride);
+        if (p >= 0 && p < a.table_rows) {
+          const float* row = a.cos_sin_table + p * D;
+#pragma unroll
+          for (int e = 0; e < E; e += 4) {
+            unpack<float>(ld_vec(row + fb + e), c + e);
+            unpack<float>(ld_vec(row + NF + fb + e), s + e);
+          }
+        } else {
+          if (lane == 0 && chunk == 0) flag(a.status, NIB_DEV_BAD_POSITION);
+#pragma unroll
+          for (int e = 0; e < E; ++e) c[e] = s[e] = 0.f;
+        }
+      } else {
+        const bool inter = a.rope_mode == NIB_ROPE_MROPE_INTERLEAVED;
+        const int s0 = a.sections[0], s1 = a.sections[1], s2 = a.sections[2];
+        __syncwarp();
+        for (int j = lane; j < NF; j += 32) {
+          int axis;
+          if (inter) {
+            const int m = j % 3;
+            axis = (m == 1 && j < 3 * s1) ? 1 : (m == 2 && j < 3 * s2) ? 2 : 0;
+          } else {
+            axis = j < s0 ? 0 : (j < s0 + s1 ? 1 : 2);
+          }
+          const int64_t p = __ldg(a.positions + axis * a.positions_axis_stride + t * a.positions_token_stride);
+          const float f = __fmul_rn(static_cast<float>(p), __ldg(a.inv_freq + j));
+          float sn, cs;
+          sincosf(f, &sn, &cs);
+          s_cos[wib][j] = round_to<T>(cs);
+          s_sin[wib][j] = round_to<T>(sn);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          c[e] = s_cos[wib][fb + e];
+          s[e] = s_sin[wib][fb + e];
+        }
+      }
+    }
+
+    // ---- per head group: norm, rotate, write
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) {
+      const int u = u0 + i;
+      if (u >= U) break;
+      if (u < Uq + Uk) {
+        const bool is_q = u < Uq;
+        const int head = is_q ? u * HPW + hs : (u - Uq) * HPW + hs;
+        const bool head_ok = head < (is_q ? nq : nkv);
+        float x[E];
+        unpack<T>(buf[i], x);
+        if (a.norm) {
+          float ss = 0.f;
+#pragma unroll
+          for (int e = 0; e < E; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
+#pragma unroll
+          for (int off = HALF; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+          const float rs = 1.0f / sqrtf(__fadd_rn(ss / static_cast<float>(D), a.eps));
+          float wf[E];
+          load_weights<T, W>(is_q ? qw : kw, l * E, wf);
+#pragma unroll
+          for (int e = 0; e < E; ++e) x[e] = round_to<T>(__fmul_rn(round_to<T>(__fmul_rn(x[e], rs)), wf[e]));
+        }
+        if (a.rope_mode != NIB_ROPE_NONE) {
+          const uint4 mine = pack<T>(x);  // exact: x already holds T values
+          uint4 other;
+          other.x = __shfl_xor_sync(0xffffffffu, mine.x, HALF);
+          other.y = __shfl_xor_sync(0xffffffffu, mine.y, HALF);
+          other.z = __shfl_xor_sync(0xffffffffu, mine.z, HALF);
+          other.w = __shfl_xor_sync(0xffffffffu, mine.w, HALF);
+          float p[E];
+          unpack<T>(other, p);
+          if (a.rope_mode == NIB_ROPE_MROPE_INTERLEAVED) {
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+              const float t1 = round_to<T>(__fmul_rn(x[e], c[e]));
+              const float t2 = round_to<T>(__fmul_rn(p[e], s[e]));
+              x[e] = round_to<T>(first ? __fsub_rn(t1, t2) : __fadd_rn(t1, t2));
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+              const float t1 = __fmul_rn(x[e], c[e]);
+              const float t2 = __fmul_rn(p[e], s[e]);
+              x[e] = first ? __fsub_rn(t1, t2) : __fadd_rn(t1, t2);
+            }
+          }
+        }
+        const uint4 o = pack<T>(x);
+        if (head_ok) {
+          if (is_q) {
+            st_vec(q_out + (t * nq + head) * D + l * E, o);
+          } else {
+            st_vec(k_out + (t * nkv + head) * D + l * E, o);
+            if (slot >= 0) st_vec(kc + slot * a.cache_slot_stride + head * D + l * E, o);
+          }
+        }
+      } else {
+        const int head = (u - Uq - Uk) * HPW + hs;
+        if (slot >= 0 && head < nkv) st_vec(vc + slot * a.cache_slot_stride + head * D + l * E, buf[i]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- generic M-RoPE apply
+// apply_multimodal_rotary_emb with given cos/sin [3, T, D] (any even D, any
+// dtypes). One thread per output element; TO is the arithmetic dtype of the
+// interleaved strategy (the promoted dtype of x and cos).
+template <typename TX, typename TC, typename TO>
+__global__ void __launch_bounds__(256)
+mrope_apply_kernel(const TX* __restrict__ x, int64_t xts, int64_t xhs, int64_t tokens,
+                   int64_t heads, int D, const TC* __restrict__ cos, const TC* __restrict__ sin,
+                   int s0, int s1, int s2, int interleaved, TX* __restrict__ out) {
+  const int64_t total = tokens * heads * D;
+  const int half = D / 2;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int d = static_cast<int>(idx % D);
+    const int64_t th = idx / D;
+    const int64_t h = th % heads;
+    const int64_t t = th / heads;
+    const int j = d % half;
+    int axis;
+    if (interleaved) {
+      const int m = j % 3;
+      axis = (m == 1 && j < 3 * s1) ? 1 : (m == 2 && j < 3 * s2) ? 2 : 0;
+    } else {
+      axis = j < s0 ? 0 : (j < s0 + s1 ? 1 : 2);
+    }
+    const int64_t ci = (axis * tokens + t) * D + d;
+    const float cv = Elem<TC>::to_f(cos[ci]);
+    const float sv = Elem<TC>::to_f(sin[ci]);
+    const TX* xr = x + t * xts + h * xhs;
+    const float xv = Elem<TX>::to_f(xr[d]);
+    const float pv = Elem<TX>::to_f(xr[d < half ? d + half : d - half]);
+    const float rot = d < half ? -pv : pv;
+    float y;
+    if (interleaved) {
+      const float t1 = round_to<TO>(__fmul_rn(xv, cv));
+      const float t2 = round_to<TO>(__fmul_rn(rot, sv));
+      y = round_to<TO>(__fadd_rn(t1, t2));
+    } else {
+      y = __fadd_rn(__fmul_rn(xv, cv), __fmul_rn(rot, sv));
+    }
+    out[idx] = Elem<TX>::from_f(y);
+  }
+}
+
+template <typename TO>
+__global__ void __launch_bounds__(256)
+mrope_cos_sin_kernel(const int64_t* __restrict__ pos, int64_t pas, int64_t pts, int64_t tokens,
+                     const float* __restrict__ inv_freq, int D, TO* __restrict__ cos,
+                     TO* __restrict__ sin) {
+  const int half = D / 2;
+  const int64_t total = 3 * tokens * half;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(idx % half);
+    const int64_t at = idx / half;
+    const int64_t t = at % tokens;
+    const int64_t ax = at / tokens;
+    const float f = __fmul_rn(static_cast<float>(__ldg(pos + ax * pas + t * pts)), __ldg(inv_freq + j));
+    float sn, cs;
+    sincosf(f, &sn, &cs);
+    const int64_t o = (ax * tokens + t) * D + j;
+    cos[o] = cos[o + half] = Elem<TO>::from_f(cs);
+    sin[o] = sin[o + half] = Elem<TO>::from_f(sn);
+  }
+}
+
+static unsigned flat_grid(int64_t total) {
+  int64_t blocks = (total + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<unsigned>(blocks);
+}
+
+template <typename T, typename W>
+static int launch_prologue(const nib_qk_prologue_args& a, cudaStream_t st) {
+  constexpr int E = Elem<T>::kPerVec;
+  const int D = a.head_dim;
+  const int lph = D / E;
+  NIB_SUPPORT(D == 64 || D == 128 || D == 256, "qk_prologue: head_dim %d not supported (64/128/256)", D);
+  NIB_SUPPORT(lph <= 32, "qk_prologue: head_dim %d too large for float32 activations", D);
+  const int hpw = 32 / lph;
+  const int Uq = (a.num_heads + hpw - 1) / hpw;
+  const int Uk = (a.num_kv_heads + hpw - 1) / hpw;
+  const int U = Uq + Uk + (a.key_cache ? Uk : 0);
+  const int64_t items = a.tokens * ((U + kChunk - 1) / kChunk);
+  int64_t blocks = (items + kPrologueWarps - 1) / kPrologueWarps;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 64;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  const unsigned nb = static_cast<unsigned>(blocks);
+  const int threads = kPrologueWarps * 32;
+  if (D == 64) qk_prologue_kernel<T, W, 64><<<nb, threads, 0, st>>>(a);
+  else if (D == 128) qk_prologue_kernel<T, W, 128><<<nb, threads, 0, st>>>(a);
+  else if constexpr (E == 8) qk_prologue_kernel<T, W, 256><<<nb, threads, 0, st>>>(a);
+  return launch_status("qk_prologue");
+}
+
+}  // namespace nib
+
+using namespace nib;
+
+extern "C" int nib_qk_prologue(const nib_qk_prologue_args* args, void* stream) {
+  NIB_REQUIRE(args != nullptr, "qk_prologue: null args");
+  NIB_REQUIRE(args->struct_size == static_cast<int32_t>(sizeof(nib_qk_prologue_args)),
+              "qk_prologue: struct_size %d does not match this library (%d)", args->struct_size,
+              static_cast<int>(sizeof(nib_qk_prologue_args)));
+  const nib_qk_prologue_args& a = *args;
+  NIB_REQUIRE(a.tokens >= 0 && a.num_heads >= 1 && a.num_kv_heads >= 1, "qk_prologue: bad sizes");
+  if (a.tokens == 0) return NIB_OK;
+  NIB_REQUIRE(a.q && a.k && a.q_out && a.k_out, "qk_prologue: null q/k pointer");
+  const int E = 16 / elem_size(a.dtype);
+  const bool store = a.key_cache != nullptr;
+  NIB_REQUIRE(!store || (a.value_cache && a.v && a.slot_mapping), "qk_prologue: store needs v, caches and slot_mapping");
+  NIB_REQUIRE(!a.norm || (a.q_weight && a.k_weight), "qk_prologue: norm needs q/k weights");
+  NIB_REQUIRE(a.rope_mode >= NIB_ROPE_NONE && a.rope_mode <= NIB_ROPE_MROPE_INTERLEAVED, "qk_prologue: bad rope mode");
+  NIB_REQUIRE(a.rope_mode == NIB_ROPE_NONE || a.positions, "qk_prologue: rope needs positions");
+  NIB_REQUIRE(a.rope_mode != NIB_ROPE_TABLE || a.cos_sin_table, "qk_prologue: table rope needs the cos/sin table");
+  if (a.rope_mode == NIB_ROPE_MROPE_CHUNKED || a.rope_mode == NIB_ROPE_MROPE_INTERLEAVED) {
+    NIB_REQUIRE(a.inv_freq, "qk_prologue: M-RoPE needs inv_freq");
+    NIB_REQUIRE(a.sections[0] > 0 && a.sections[1] > 0 && a.sections[2] > 0 &&
+                    a.sections[0] + a.sections[1] + a.sections[2] == a.head_dim / 2,
+                "qk_prologue: sections must be positive and sum to head_dim/2");
+  }
+  const void* vec_ptrs[] = {a.q, a.k, a.q_out, a.k_out, store ? a.v : a.q,
+                            store ? a.key_cache : a.q, store ? a.value_cache : a.q};
+  for (const void* p : vec_ptrs) NIB_SUPPORT(aligned16(p), "qk_prologue: tensors must be 16-byte aligned");
+  const int64_t strides[] = {a.q_token_stride, a.q_head_stride, a.k_token_stride, a.k_head_stride,
+                             store ? a.v_token_stride : 0, store ? a.v_head_stride : 0,
+                             store ? a.cache_slot_stride : 0};
+  for (int64_t s : strides) NIB_SUPPORT(s % E == 0, "qk_prologue: strides must be multiples of %d elements", E);
+  if (a.rope_mode == NIB_ROPE_TABLE) NIB_SUPPORT(aligned16(a.cos_sin_table), "qk_prologue: table must be 16-byte aligned");
+  if (a.norm) NIB_SUPPORT(aligned16(a.q_weight) && aligned16(a.k_weight), "qk_prologue: weights must be 16-byte aligned");
+  const cudaStream_t st = as_stream(stream);
+  NIB_DISPATCH(a.dtype, T, {
+    if (!a.norm || a.weight_dtype == a.dtype) return launch_prologue<T, T>(a, st);
+    if (a.weight_dtype == NIB_F32) return launch_prologue<T, float>(a, st);
+    set_error("qk_prologue: weight dtype must equal the activation dtype or be float32");
+    return NIB_ERR_UNSUPPORTED;
+  });
+  return NIB_OK;
+}
+
+extern "C" int nib_mrope_apply(int x_dtype, const void* x, int64_t x_token_stride,
+                               int64_t x_head_stride, int64_t tokens, int64_t heads, int64_t head_dim,
+                               int cos_dtype, const void* cos, const void* sin,
+                               const int32_t sections[3], int interleaved, void* out, void* stream) {
+  NIB_REQUIRE(tokens >= 0 && heads >= 1 && head_dim >= 2 && head_dim % 2 == 0, "mrope_apply: bad sizes");
+  if (tokens == 0) return NIB_OK;
+  NIB_REQUIRE(x && cos && sin && out && sections, "mrope_apply: null pointer");
+  const int64_t total = tokens * heads * head_dim;
+  const cudaStream_t st = as_stream(stream);
+  const unsigned grid = flat_grid(total);
+  const int D = static_cast<int>(head_dim);
+#define NIB_MROPE_APPLY(TX, TC, TO)                                                              \
+  mrope_apply_kernel<TX, TC, TO><<<grid, 256, 0, st>>>(                                          \
+      static_cast<const TX*>(x), x_token_stride, x_head_stride, tokens, heads, D,                \
+      static_cast<const TC*>(cos), static_cast<const TC*>(sin), sections[0], sections[1],        \
+      sections[2], interleaved, static_cast<TX*>(out))
+  NIB_DISPATCH(x_dtype, TX, {
+    if (cos_dtype == x_dtype) {
+      NIB_MROPE_APPLY(TX, TX, TX);
+    } else if (cos_dtype == NIB_F32) {
+      NIB_MROPE_APPLY(TX, float, float);
+    } else if (cos_dtype == NIB_F16) {
+      NIB_MROPE_APPLY(TX, __half, float);
+    } else if (cos_dtype == NIB_BF16) {
+      NIB_MROPE_APPLY(TX, __nv_bfloat16, float);
+    } else {
+      set_error("mrope_apply: bad cos dtype %d", cos_dtype);
+      return NIB_ERR_UNSUPPORTED;
+    }
+  });
+#undef NIB_MROPE_APPLY
+  return launch_status("mrope_apply");
+}
+
+extern "C" int nib_mrope_cos_sin(const int64_t* positions, int64_t positions_axis_stride,
+                                 int64_t positions_token_stride, int64_t tokens,
+                                 const float* inv_freq, int64_t head_dim, int out_dtype, void* cos,
+                                 void* sin, void* stream) {
+  NIB_REQUIRE(tokens >= 0 && head_dim >= 2 && head_dim % 2 == 0, "mrope_cos_sin: bad sizes");
+  if (tokens == 0) return NIB_OK;
+  NIB_REQUIRE(positions && inv_freq && cos && sin, "mrope_cos_sin: null pointer");
+  const cudaStream_t st = as_stream(stream);
+  const unsigned grid = flat_grid(3 * tokens * (head_dim / 2));
+  NIB_DISPATCH(out_dtype, TO,
+               mrope_cos_sin_kernel<TO><<<grid, 256, 0, st>>>(
+                   positions, positions_axis_stride, positions_token_stride, tokens, inv_freq,
+                   static_cast<int>(head_dim), static_cast<TO*>(cos), static_cast<TO*>(sin)));
+  return launch_status("mrope_cos_sin");
+}

@@ -1,0 +1,79 @@
+"""Attention-side pieces of the hot path: the paged KV store and the fused
+attention prologue.
+
+``store_kvcache`` keeps the signature of ``nanovllm/layers/attention.py:10-33``.
+``attention_prologue`` replaces, in one kernel launch, the sequence the
+decoder layers run between the qkv projection and the attention kernel:
+
+* Qwen3       ``nanovllm/models/qwen3.py:77-86``       split, q/k RMSNorm, 1-D RoPE, store
+* Qwen3-VL    ``nanovllm/models/qwen3_vl.py:161-172``  split, q/k text norm, interleaved M-RoPE, store
+* Qwen2.5-VL  ``nanovllm/models/qwen25_vl.py:66-76``   split, chunked M-RoPE, store
+
+It returns the rotated q and k (prefill attention without a block table reads
+them directly, ``attention.py:99-116``) and the v view; the caches are already
+written, so the caller's attention must skip its own store.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from nano_vllm_multimodal_b200 import ops
+from nano_vllm_multimodal_b200.layers.paged_kv.base import validate_store_inputs
+
+
+def store_kvcache(key, value, k_cache, v_cache, slot_mapping) -> None:
+    """Write this step's K/V rows into the paged caches (slot -1 = skip)."""
+    validate_store_inputs(key, value, k_cache, v_cache, slot_mapping)
+    ops.paged_store(key, value, k_cache, v_cache, slot_mapping)
+
+
+def _rope_args(rotary_emb):
+    if hasattr(rotary_emb, "cos_sin_cache"):
+        return dict(rope_mode=ops.ROPE_TABLE, cos_sin_cache=rotary_emb.cos_sin_cache)
+    if hasattr(rotary_emb, "inv_freq") and hasattr(rotary_emb, "sections"):
+        mode = (ops.ROPE_MROPE_INTERLEAVED if rotary_emb.strategy == "interleaved"
+                else ops.ROPE_MROPE_CHUNKED)
+        return dict(rope_mode=mode, inv_freq=rotary_emb.inv_freq, sections=tuple(rotary_emb.sections))
+    raise TypeError(f"unsupported rotary embedding module {type(rotary_emb).__name__}")
+
+
+def attention_prologue(qkv: torch.Tensor, *, num_heads: int, num_kv_heads: int, head_dim: int,
+                       positions: torch.Tensor, rotary_emb, q_norm=None, k_norm=None,
+                       k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,
+                       slot_mapping: torch.Tensor | None = None):
+    """Fused q/k norm + rotary + paged store -> ``(q, k, v)``.
+
+    ``q_norm``/``k_norm`` are RMSNorm-like modules (``weight``, ``eps``) or
+    ``None``; ``rotary_emb`` is a ``RotaryEmbedding`` (table) or a
+    ``MultimodalRotaryEmbedding``. The store runs when both caches are
+    non-empty, as in ``Attention.forward`` (``attention.py:87-93``).
+    """
+    q_size, kv_size = num_heads * head_dim, num_kv_heads * head_dim
+    q, k, v = qkv.split([q_size, kv_size, kv_size], dim=-1)
+    q = q.view(-1, num_heads, head_dim)
+    k = k.view(-1, num_kv_heads, head_dim)
+    v = v.view(-1, num_kv_heads, head_dim)
+    store = k_cache is not None and v_cache is not None and k_cache.numel() and v_cache.numel()
+    if store:
+        validate_store_inputs(k, v, k_cache, v_cache, slot_mapping)
+    if (q_norm is None) != (k_norm is None):
+        raise ValueError("q_norm and k_norm must be given together")
+    if not ops.prologue_supported(q, k, v if store else None):
+        # unusual head size / layout: the same stages as separate kernels
+        if q_norm is not None:
+            q, k = q_norm(q), k_norm(k)
+        q, k = rotary_emb(positions, q, k)
+        if store:
+            ops.paged_store(k, v, k_cache, v_cache, slot_mapping)
+        return q, k, v
+    if positions.dtype != torch.long:
+        positions = positions.long()
+    norm = {}
+    if q_norm is not None:
+        norm = dict(q_weight=q_norm.weight, k_weight=k_norm.weight, eps=q_norm.eps)
+    cache = {}
+    if store:
+        cache = dict(v=v, key_cache=k_cache, value_cache=v_cache, slot_mapping=slot_mapping)
+    q_rot, k_rot = ops.qk_prologue(q, k, positions=positions, **norm, **_rope_args(rotary_emb), **cache)
+    return q_rot, k_rot, v

@@ -32,6 +32,7 @@ __all__ = [
     "apply_mrope",
     "mrope_forward",
     "paged_store",
+    "paged_store_",
     "paged_gather",
     "embedding",
     "add_deepstack_rows",
@@ -271,6 +272,16 @@ def paged_store(key, value, key_cache, value_cache, slot_mapping):
     return out[0], out[1]
 
 
+def paged_store_(key, value, key_cache, value_cache, slot_mapping):
+    """In-place form of the same store, as the reference's PyTorch backend runs
+    it (``pytorch_backend.py:34-38``: ``index_copy_`` of the valid rows into the
+    flattened caches). Used where the caches are too large to copy."""
+    valid = slot_mapping >= 0
+    slots = slot_mapping[valid].to(dtype=torch.long)
+    key_cache.flatten(0, 1).index_copy_(0, slots, key[valid])
+    value_cache.flatten(0, 1).index_copy_(0, slots, value[valid])
+
+
 def paged_gather(cache, block_table, sequence_length):
     """Paged-KV gather: ``nanovllm/layers/paged_kv/pytorch_backend.py:40-50``.
 
@@ -330,6 +341,7 @@ def qk_norm_rope_store(
     key_cache=None,
     value_cache=None,
     slot_mapping=None,
+    inplace=False,
 ):
     """The attention prologue that the fused kernel replaces.
 
@@ -347,7 +359,8 @@ def qk_norm_rope_store(
     (RMSNorm), ``"text"`` (Qwen3VLTextRMSNorm) or ``None``. The store writes
     the rotated k and the raw v (``nanovllm/layers/attention.py:87-93``).
     Returns ``(q, k, key_cache, value_cache)`` (caches are new tensors, or
-    ``None`` when not given).
+    ``None`` when not given; with ``inplace=True`` the given caches are
+    updated and returned).
     """
     q_size = num_heads * head_dim
     kv_size = num_kv_heads * head_dim
@@ -366,7 +379,11 @@ def qk_norm_rope_store(
         q, k = mrope_forward(positions, q, k, inv_freq, sections, strategy)
     kc = vc = None
     if key_cache is not None:
-        kc, vc = paged_store(k, v, key_cache, value_cache, slot_mapping)
+        if inplace:
+            paged_store_(k, v, key_cache, value_cache, slot_mapping)
+            kc, vc = key_cache, value_cache
+        else:
+            kc, vc = paged_store(k, v, key_cache, value_cache, slot_mapping)
     return q, k, kc, vc
 
 
@@ -391,6 +408,7 @@ def qwen3_vl_fused_layer(
     key_cache,
     value_cache,
     slot_mapping,
+    inplace=False,
 ):
     """One decoder layer's elementwise work with the GEMM outputs supplied.
 
@@ -405,7 +423,7 @@ def qwen3_vl_fused_layer(
         qkv, num_heads, num_kv_heads, head_dim,
         positions=positions, rope=("mrope", inv_freq, sections, "interleaved"),
         q_weight=q_weight, k_weight=k_weight, eps=eps, norm="text",
-        key_cache=key_cache, value_cache=value_cache, slot_mapping=slot_mapping,
+        key_cache=key_cache, value_cache=value_cache, slot_mapping=slot_mapping, inplace=inplace,
     )
     y2, h2 = add_text_rms_norm(attn_out, h1, w_post, eps)
     act = silu_and_mul(gate_up)
