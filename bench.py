@@ -74,6 +74,8 @@ def parse_args(argv=None):
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    p.add_argument("--cache-blocks", type=int, default=CACHE_BLOCKS,
+                   help="blocks of 256 slots per K/V cache per GPU (smaller only for profiler captures)")
     return p.parse_args(argv)
 
 
@@ -187,7 +189,7 @@ def summarize_clocks(lines: list[str]) -> dict | None:
 # ------------------------------------------------------------------ GPU workload
 
 
-def make_rank_inputs(rank: int, world: int, tokens_total: int, device):
+def make_rank_inputs(rank: int, world: int, tokens_total: int, device, cache_blocks: int = CACHE_BLOCKS):
     from nano_vllm_multimodal_b200 import workloads as W
 
     t0, T = shard(tokens_total, rank, world)
@@ -202,14 +204,14 @@ def make_rank_inputs(rank: int, world: int, tokens_total: int, device):
         "w_in": n((H,), 1.0, 0.1), "w_post": n((H,), 1.0, 0.1),
         "q_weight": n((D,), 1.0, 0.1), "k_weight": n((D,), 1.0, 0.1),
         "positions": torch.randint(0, 32768, (3, T), generator=seeds(), device=device),
-        "slot_mapping": torch.randperm(CACHE_BLOCKS * 256, generator=seeds(), device=device)[:T].to(torch.int32),
+        "slot_mapping": torch.randperm(cache_blocks * 256, generator=seeds(), device=device)[:T].to(torch.int32),
         "inv_freq": (1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).to(device),
     }
-    cache_shape = (CACHE_BLOCKS, 256, NKV, D)
+    cache_shape = (cache_blocks, 256, NKV, D)
     inp["key_cache"] = torch.full(cache_shape, -3.0, dtype=torch.bfloat16, device=device)
     inp["value_cache"] = torch.full(cache_shape, -3.0, dtype=torch.bfloat16, device=device)
     need = GATHER_LEN // 256
-    inp["tables"] = torch.stack([torch.randperm(CACHE_BLOCKS, generator=seeds(), device=device)[:need]
+    inp["tables"] = torch.stack([torch.randperm(cache_blocks, generator=seeds(), device=device)[:need]
                                  for _ in range(S)]).to(torch.int32) if S else \
         torch.empty(0, need, dtype=torch.int32, device=device)
     inp["seq_lens"] = torch.full((S,), GATHER_LEN, dtype=torch.int32, device=device)
@@ -389,7 +391,7 @@ def config_block(args, world, extra=None):
            "heads": [NQ, NKV], "head_dim": D, "intermediate": INTER,
            "mrope": {"strategy": "interleaved", "sections": list(SECTIONS), "theta": THETA},
            "gather": {"sequences": GATHER_SEQS, "tokens_per_sequence": GATHER_LEN, "caches": 2},
-           "cache_per_gpu": [CACHE_BLOCKS, 256, NKV, D], "parallelism": f"token-sharded x{world}",
+           "cache_per_gpu": [args.cache_blocks, 256, NKV, D], "parallelism": f"token-sharded x{world}",
            "value_counts": "token x fused-layer passes per second",
            "l2": "inputs larger than L2 (every kernel's working set > 126 MB at every N)"}
     if extra:
@@ -436,7 +438,9 @@ def ours_arm(args, rank, world, local):
 
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
-    inp = make_rank_inputs(rank, world, args.tokens, device)
+    if args.cache_blocks * 256 < -(-args.tokens // world) or args.cache_blocks < GATHER_LEN // 256:
+        raise SystemExit("bench.py: --cache-blocks too small for the tokens per rank / gather length")
+    inp = make_rank_inputs(rank, world, args.tokens, device, args.cache_blocks)
     T = inp["tokens"]
     torch.cuda.synchronize()
 

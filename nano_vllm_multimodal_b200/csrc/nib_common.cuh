@@ -152,6 +152,23 @@ __device__ __forceinline__ void load_weights(const W* w, int64_t i, float* f) {
   }
 }
 
+// Sum of squares of one 16-byte vector's E values: squares rounded to fp32,
+// then a pairwise tree ((s0+s1)+(s2+s3))+... . This is the fixed summation
+// order of every RMSNorm statistic in this library (lanes then add their
+// vectors' sums in order and combine by an xor butterfly).
+template <int E>
+__device__ __forceinline__ float sumsq_tree(const float* v) {
+  float s[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) s[e] = __fmul_rn(v[e], v[e]);
+#pragma unroll
+  for (int w = E / 2; w >= 1; w /= 2) {
+#pragma unroll
+    for (int e = 0; e < w; ++e) s[e] = __fadd_rn(s[2 * e], s[2 * e + 1]);
+  }
+  return s[0];
+}
+
 __device__ __forceinline__ void flag(unsigned int* status, unsigned int bit) {
   if (status != nullptr) atomicOr(status, bit);
 }

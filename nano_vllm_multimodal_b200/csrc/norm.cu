@@ -6,9 +6,10 @@
 //   var = mean(s^2)                 fp32
 //   n   = dtype(s * (1/sqrt(var + eps)))
 //   y   = dtype(n * w)              one more rounding
-// The 1/sqrt is the IEEE sqrt followed by the IEEE divide (what PyTorch's CPU
-// rsqrt computes); squares are rounded before they are summed, as
-// `x.pow(2).mean()` does. Only the summation order differs from PyTorch.
+// The 1/sqrt is the IEEE sqrt followed by the IEEE divide; squares are rounded
+// before they are summed, as `x.pow(2).mean()` does. The summation order is
+// fixed (sumsq_tree per 16-byte vector, vectors in order per lane, lanes by
+// xor butterfly, warps in order); PyTorch leaves its order unspecified.
 //
 // Layout: rows of n elements, each row read once with 16-byte vectors and
 // written once. Rows of up to 256 vectors (2048 bf16) live in one warp's
@@ -62,8 +63,7 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
           v[i][e] = round_sum ? round_to<T>(s) : s;
         }
       }
-#pragma unroll
-      for (int e = 0; e < E; ++e) ss = __fadd_rn(ss, __fmul_rn(v[i][e], v[i][e]));
+      ss = __fadd_rn(ss, sumsq_tree<E>(v[i]));
     }
 #pragma unroll
     for (int off = G / 2; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
@@ -120,8 +120,7 @@ rms_rows_block(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __r
           v[i][e] = round_sum ? round_to<T>(s) : s;
         }
       }
-#pragma unroll
-      for (int e = 0; e < E; ++e) ss = __fadd_rn(ss, __fmul_rn(v[i][e], v[i][e]));
+      ss = __fadd_rn(ss, sumsq_tree<E>(v[i]));
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));

@@ -21,6 +21,7 @@
 // are computed once per item for the head_dim/2 frequencies (each lane handles
 // head_dim/64 of them) and shared through shared memory.
 #include "dispatch.cuh"
+#include "prologue.cuh"
 
 namespace nib {
 
@@ -159,12 +160,10 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
         float x[E];
         unpack<T>(buf[i], x);
         if (a.norm) {
-          float ss = 0.f;
-#pragma unroll
-          for (int e = 0; e < E; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
+          float ss = sumsq_tree<E>(x);
 #pragma unroll
           for (int off = HALF; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-          const float rs = 1.0f / sqrtf(__fadd_rn(ss / static_cast<float>(D), a.eps));
+          const float rs = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / D), a.eps));
           float wf[E];
           load_weights<T, W>(is_q ? qw : kw, l * E, wf);
 #pragma unroll
@@ -237,7 +236,10 @@ mrope_apply_kernel(const TX* __restrict__ x, int64_t xts, int64_t xhs, int64_t t
     } else {
       axis = j < s0 ? 0 : (j < s0 + s1 ? 1 : 2);
     }
-    const int64_t ci = (axis * tokens + t) * D + d;
+    // chunked selects over the full head dim (sections repeated), so element d
+    // reads column d; interleaved selects on the first half and repeats that
+    // selection for the second half, so both halves read column j
+    const int64_t ci = (axis * tokens + t) * D + (interleaved ? j : d);
     const float cv = Elem<TC>::to_f(cos[ci]);
     const float sv = Elem<TC>::to_f(sin[ci]);
     const TX* xr = x + t * xts + h * xhs;
@@ -346,6 +348,12 @@ extern "C" int nib_qk_prologue(const nib_qk_prologue_args* args, void* stream) {
   if (a.rope_mode == NIB_ROPE_TABLE) NIB_SUPPORT(aligned16(a.cos_sin_table), "qk_prologue: table must be 16-byte aligned");
   if (a.norm) NIB_SUPPORT(aligned16(a.q_weight) && aligned16(a.k_weight), "qk_prologue: weights must be 16-byte aligned");
   const cudaStream_t st = as_stream(stream);
+  NIB_REQUIRE(a.variant >= 0 && a.variant <= 2, "qk_prologue: bad variant %d", a.variant);
+  const bool pipe_ok = prologue_pipe_eligible(a);
+  NIB_SUPPORT(a.variant != 2 || pipe_ok, "qk_prologue: the pipelined variant needs q/k/v as consecutive "
+              "head ranges of one 16-byte aligned bf16/fp16 row");
+  if (a.variant == 2 || (a.variant == 0 && pipe_ok && a.tokens >= kPipeMinTokens))
+    return launch_prologue_pipe(a, st);
   NIB_DISPATCH(a.dtype, T, {
     if (!a.norm || a.weight_dtype == a.dtype) return launch_prologue<T, T>(a, st);
     if (a.weight_dtype == NIB_F32) return launch_prologue<T, float>(a, st);

@@ -154,7 +154,7 @@ std::tuple<Tensor, Tensor> qk_prologue(const Tensor& q, const Tensor& k, const o
                                        const optional<Tensor>& key_cache,
                                        const optional<Tensor>& value_cache,
                                        const optional<Tensor>& slot_mapping,
-                                       const optional<Tensor>& status) {
+                                       const optional<Tensor>& status, int64_t variant) {
   TORCH_CHECK(q.dim() == 3 && k.dim() == 3, "qk_prologue: q and k must be [tokens, heads, head_dim]");
   TORCH_CHECK(q.size(0) == k.size(0) && q.size(2) == k.size(2), "qk_prologue: q/k shape mismatch");
   TORCH_CHECK(q.scalar_type() == k.scalar_type(), "qk_prologue: q and k dtypes differ");
@@ -243,6 +243,7 @@ std::tuple<Tensor, Tensor> qk_prologue(const Tensor& q, const Tensor& k, const o
     a.cache_slot_stride = kc.stride(1);
   }
   a.status = status_ptr(status);
+  a.variant = static_cast<int32_t>(variant);
   check(nib_qk_prologue(&a, stream_of(q)), "nanoinfer_b200::qk_prologue");
   return {qo, ko};
 }
@@ -567,7 +568,7 @@ TORCH_LIBRARY(nanoinfer_b200, m) {
   m.def("qk_prologue(Tensor q, Tensor k, Tensor? v, Tensor? positions, Tensor? q_weight, "
         "Tensor? k_weight, float eps, int rope_mode, Tensor? cos_sin_cache, Tensor? inv_freq, "
         "int[] sections, Tensor(a!)? key_cache, Tensor(b!)? value_cache, Tensor? slot_mapping, "
-        "Tensor(c!)? status) -> (Tensor, Tensor)");
+        "Tensor(c!)? status, int variant=0) -> (Tensor, Tensor)");
   m.def("mrope_apply(Tensor x, Tensor cos, Tensor sin, int[] sections, bool interleaved) -> Tensor");
   m.def("mrope_cos_sin(Tensor positions, Tensor inv_freq, ScalarType dtype) -> (Tensor, Tensor)");
   m.def("paged_gather_varlen(Tensor cache, Tensor block_tables, Tensor seq_lens, Tensor cu_seqlens, "

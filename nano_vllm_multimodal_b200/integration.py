@@ -1,0 +1,89 @@
+"""Swap this package's kernels into an installed NanoInfer (``nanovllm``).
+
+``install()`` rebinds, inside the already-importable ``nanovllm`` package, the
+hot-path names that the decoder models import at module load:
+
+* ``nanovllm.layers.layernorm.RMSNorm``
+* ``nanovllm.layers.activation.SiluAndMul``
+* ``nanovllm.layers.rotary_embedding.{RotaryEmbedding, get_rope, apply_rotary_emb}``
+* ``nanovllm.layers.multimodal_rotary_embedding.{MultimodalRotaryEmbedding,
+  apply_multimodal_rotary_emb}``
+* ``nanovllm.layers.embed_head.VocabParallelEmbedding``
+* ``nanovllm.layers.attention.store_kvcache``
+* ``nanovllm.models.qwen3_vl.Qwen3VLTextRMSNorm`` and
+  ``Qwen3VLLanguageModel._add_deepstack_rows``
+* ``nanovllm.layers.paged_kv.loader.load_paged_kv_extension`` - so the
+  reference's own ``CUDAPagedKVBackend`` gets ``torch.ops.nanovllm_paged_kv``
+  and ``PagedKVCache`` from this package's extension instead of JIT-building
+  its sources; ``ModelRunner`` then runs unchanged with
+  ``paged_kv_backend="cuda"``.
+
+Call it before ``nanovllm.models.*`` is imported (the models bind the layer
+classes at import time); already-imported model modules are patched too when
+they hold the names. Returns the list of rebound ``module.attribute`` names.
+"""
+
+from __future__ import annotations
+
+import importlib
+import sys
+
+
+def _targets():
+    from nano_vllm_multimodal_b200._lib import load_ops
+    from nano_vllm_multimodal_b200.layers import activation, attention, embed_head, layernorm
+    from nano_vllm_multimodal_b200.layers import multimodal_rotary_embedding as mrope
+    from nano_vllm_multimodal_b200.layers import qwen3_vl, rotary_embedding
+
+    def load_paged_kv_extension(*, verbose: bool = False) -> None:
+        load_ops()
+
+    return {
+        "nanovllm.layers.layernorm": {"RMSNorm": layernorm.RMSNorm},
+        "nanovllm.layers.activation": {"SiluAndMul": activation.SiluAndMul},
+        "nanovllm.layers.rotary_embedding": {"RotaryEmbedding": rotary_embedding.RotaryEmbedding,
+                                             "get_rope": rotary_embedding.get_rope,
+                                             "apply_rotary_emb": rotary_embedding.apply_rotary_emb},
+        "nanovllm.layers.multimodal_rotary_embedding": {
+            "MultimodalRotaryEmbedding": mrope.MultimodalRotaryEmbedding,
+            "apply_multimodal_rotary_emb": mrope.apply_multimodal_rotary_emb},
+        "nanovllm.layers.embed_head": {"VocabParallelEmbedding": embed_head.VocabParallelEmbedding},
+        "nanovllm.layers.attention": {"store_kvcache": attention.store_kvcache},
+        "nanovllm.layers.paged_kv.loader": {"load_paged_kv_extension": load_paged_kv_extension},
+        "nanovllm.layers.paged_kv.cuda_backend": {"load_paged_kv_extension": load_paged_kv_extension},
+        "nanovllm.models.qwen3_vl": {"Qwen3VLTextRMSNorm": qwen3_vl.Qwen3VLTextRMSNorm},
+    }
+
+
+# names a model module imports from the layer modules above
+_MODEL_MODULES = ("nanovllm.models.qwen3", "nanovllm.models.qwen25_vl", "nanovllm.models.qwen3_vl")
+
+
+def install() -> list[str]:
+    from nano_vllm_multimodal_b200.layers import qwen3_vl
+
+    targets = _targets()
+    done = []
+    for mod_name, names in targets.items():
+        try:
+            mod = importlib.import_module(mod_name)
+        except ImportError:
+            continue
+        for attr, obj in names.items():
+            if hasattr(mod, attr):
+                setattr(mod, attr, obj)
+                done.append(f"{mod_name}.{attr}")
+    flat = {attr: obj for names in targets.values() for attr, obj in names.items()}
+    for mod_name in _MODEL_MODULES:
+        mod = sys.modules.get(mod_name)
+        if mod is None:
+            continue
+        for attr, obj in flat.items():
+            if hasattr(mod, attr) and f"{mod_name}.{attr}" not in done:
+                setattr(mod, attr, obj)
+                done.append(f"{mod_name}.{attr}")
+    lm = sys.modules.get("nanovllm.models.qwen3_vl")
+    if lm is not None and hasattr(lm, "Qwen3VLLanguageModel"):
+        lm.Qwen3VLLanguageModel._add_deepstack_rows = staticmethod(qwen3_vl.add_deepstack_rows)
+        done.append("nanovllm.models.qwen3_vl.Qwen3VLLanguageModel._add_deepstack_rows")
+    return done

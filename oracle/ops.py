@@ -46,9 +46,98 @@ def _round(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
 
 
 # --------------------------------------------------------------------------- norms
+#
+# ``order`` selects how the fp32 statistics mean(x^2) and 1/sqrt(var + eps) are
+# evaluated. "torch" runs the reference's own ops (``x.pow(2).mean()`` and
+# ``torch.rsqrt``) as this CPU build executes them. "kernel" evaluates the SAME
+# formula with an explicit order: squares rounded to fp32; the squares of each
+# 16-byte vector summed as a pairwise tree ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7));
+# a lane adds its vectors' sums in order; lanes combined by an xor butterfly
+# (and, for rows longer than 256 vectors, warps summed in order); then IEEE
+# ``sum / n``, ``+ eps``, ``sqrt`` and ``1 / .`` - the order the CUDA kernels
+# use. Any fp32 summation order is a valid evaluation of ``mean``; fixing one
+# makes the kernels checkable bit-for-bit. Everything after the statistics is
+# identical.
 
 
-def add_rms_norm(x, residual, weight, eps):
+def _vec_elems(dtype):
+    return 16 // torch.empty((), dtype=dtype).element_size()
+
+
+def _vector_sums(sq, vec):
+    """Pairwise-tree sum of the squares inside each 16-byte vector -> [rows, n/vec]."""
+    v = sq.reshape(sq.shape[0], -1, vec)
+    while v.shape[-1] > 1:
+        v = (v[..., 0::2] + v[..., 1::2]).astype(np.float32)
+    return v[..., 0]
+
+
+def _lanes_sumsq(sq, nv, vec, lanes, vpt):
+    rows = sq.shape[0]
+    vs = _vector_sums(sq, vec)
+    acc = np.zeros((rows, lanes), np.float32)
+    lane = np.arange(lanes)
+    for i in range(vpt):
+        vi = i * lanes + lane
+        ok = vi < nv
+        acc[:, ok] = acc[:, ok] + vs[:, vi[ok]]
+    off = lanes // 2
+    while off >= 1:
+        acc = acc + acc[:, lane ^ off]
+        off //= 2
+    return acc[:, 0]
+
+
+def _block_sumsq(sq, nv, vec, threads, vpt=4):
+    rows = sq.shape[0]
+    vs = _vector_sums(sq, vec)
+    acc = np.zeros((rows, threads), np.float32)
+    th = np.arange(threads)
+    for i in range(vpt):
+        vi = i * threads + th
+        ok = vi < nv
+        acc[:, ok] = acc[:, ok] + vs[:, vi[ok]]
+    off = 16
+    while off >= 1:
+        acc = acc + acc[:, th ^ off]
+        off //= 2
+    tot = np.zeros(rows, np.float32)
+    for w in range(threads // 32):
+        tot = tot + acc[:, w * 32]
+    return tot
+
+
+def kernel_sumsq(s32, vec, add):
+    """Sum of squares of each row of ``s32`` ([rows, n] fp32 numpy) in the
+    kernels' order (``nano_vllm_multimodal_b200/csrc/norm.cu`` launch rules:
+    <= 16 vectors and no residual -> one power-of-two lane group; <= 256
+    vectors -> 32 lanes; longer rows -> one CTA, 4 vectors per thread)."""
+    rows, n = s32.shape
+    nv = n // vec
+    sq = (s32 * s32).astype(np.float32)
+    if nv <= 16 and not add:
+        lanes = 1
+        while lanes < nv:
+            lanes *= 2
+        return _lanes_sumsq(sq, nv, vec, lanes, 1)
+    if nv <= 256:
+        return _lanes_sumsq(sq, nv, vec, 32, -(-nv // 32))
+    threads = -(-(-(-nv // 4)) // 32) * 32
+    return _block_sumsq(sq, nv, vec, threads)
+
+
+def _inv_rms(s, eps, order, dtype, add=False):
+    """1/sqrt(mean(s^2) + eps) for fp32 ``s`` [..., n], keepdim."""
+    if order == "torch":
+        return torch.rsqrt(s.pow(2).mean(dim=-1, keepdim=True) + eps)
+    n = s.shape[-1]
+    rows = s.reshape(-1, n).contiguous().numpy()
+    ss = kernel_sumsq(rows, _vec_elems(dtype), add)
+    r = np.float32(1.0) / np.sqrt(ss / np.float32(n) + np.float32(eps))
+    return torch.from_numpy(r.astype(np.float32)).reshape(*s.shape[:-1], 1)
+
+
+def add_rms_norm(x, residual, weight, eps, order="torch"):
     """Fused residual add + RMSNorm.
 
     Follows ``nanovllm/layers/layernorm.py:28-40`` (``add_rms_forward``): the sum
@@ -60,25 +149,23 @@ def add_rms_norm(x, residual, weight, eps):
     dtype = x.dtype
     s = x.float() + residual.float()
     res_out = _round(s, dtype)
-    var = s.pow(2).mean(dim=-1, keepdim=True)
-    n = _round(s * torch.rsqrt(var + eps), dtype)
+    n = _round(s * _inv_rms(s, eps, order, dtype, add=True), dtype)
     y = _round(n.float() * weight.float(), dtype)
     return y, res_out
 
 
-def rms_norm(x, weight, eps):
+def rms_norm(x, weight, eps, order="torch"):
     """RMSNorm without residual: ``nanovllm/layers/layernorm.py:16-26``.
 
     Output is a new tensor (``x.float()`` copies), laid out contiguously.
     """
     dtype = x.dtype
     xf = x.float()
-    var = xf.pow(2).mean(dim=-1, keepdim=True)
-    n = _round(xf * torch.rsqrt(var + eps), dtype)
+    n = _round(xf * _inv_rms(xf, eps, order, dtype), dtype)
     return _round(n.float() * weight.float(), dtype).contiguous()
 
 
-def text_rms_norm(x, weight, eps):
+def text_rms_norm(x, weight, eps, order="torch"):
     """``Qwen3VLTextRMSNorm.forward``: ``nanovllm/models/qwen3_vl.py:74-79``.
 
     ``weight * normalized.to(input_dtype)``: the product is taken in the
@@ -87,13 +174,12 @@ def text_rms_norm(x, weight, eps):
     """
     dtype = x.dtype
     xf = x.float()
-    var = xf.pow(2).mean(-1, keepdim=True)
-    n = _round(xf * torch.rsqrt(var + eps), dtype)
+    n = _round(xf * _inv_rms(xf, eps, order, dtype), dtype)
     out_dtype = torch.promote_types(weight.dtype, dtype)
     return _round(weight.float() * n.float(), out_dtype).contiguous()
 
 
-def add_text_rms_norm(x, residual, weight, eps):
+def add_text_rms_norm(x, residual, weight, eps, order="torch"):
     """Qwen3-VL residual add then text RMSNorm.
 
     ``nanovllm/models/qwen3_vl.py:232-237``: ``hidden_states + residual`` is a
@@ -102,7 +188,12 @@ def add_text_rms_norm(x, residual, weight, eps):
     Returns ``(normed, rounded_sum)``.
     """
     s = _round(x.float() + residual.float(), x.dtype)
-    return text_rms_norm(s, weight, eps), s
+    if order == "torch":
+        return text_rms_norm(s, weight, eps), s
+    sf = s.float()
+    n = _round(sf * _inv_rms(sf, eps, order, x.dtype, add=True), x.dtype)
+    out_dtype = torch.promote_types(weight.dtype, x.dtype)
+    return _round(weight.float() * n.float(), out_dtype).contiguous(), s
 
 
 # --------------------------------------------------------------------------- activation
@@ -342,6 +433,7 @@ def qk_norm_rope_store(
     value_cache=None,
     slot_mapping=None,
     inplace=False,
+    order="torch",
 ):
     """The attention prologue that the fused kernel replaces.
 
@@ -369,9 +461,9 @@ def qk_norm_rope_store(
     k = k.reshape(-1, num_kv_heads, head_dim)
     v = v.reshape(-1, num_kv_heads, head_dim)
     if norm == "rms":
-        q, k = rms_norm(q, q_weight, eps), rms_norm(k, k_weight, eps)
+        q, k = rms_norm(q, q_weight, eps, order), rms_norm(k, k_weight, eps, order)
     elif norm == "text":
-        q, k = text_rms_norm(q, q_weight, eps), text_rms_norm(k, k_weight, eps)
+        q, k = text_rms_norm(q, q_weight, eps, order), text_rms_norm(k, k_weight, eps, order)
     if rope[0] == "table":
         q, k = apply_rope(positions, q, k, rope[1])
     else:

@@ -1,10 +1,11 @@
 """Fused q/k norm + RoPE/M-RoPE + paged store vs the reference's composition.
 
 The oracle runs the reference's stage order on the CPU (split views, per-head
-norm rounded to the dtype, rotation, store of rotated k and raw v). Cache
-placement and untouched slots are bit-exact; the rotated q/k follow the
-tolerances of ``test_gpu_rope.py`` (bit-exact for the 1-D table, and for
-M-RoPE bit-exact given the kernel's own cos/sin)."""
+norm rounded to the dtype, rotation, store of rotated k and raw v), with the
+norm statistics in the kernels' fp32 summation order (``order="kernel"``; the
+norm tests bound the difference to PyTorch's own order). With that, the fused
+kernel is bit-exact: q, k, cache placement, untouched slots - for M-RoPE given
+the kernel's own cos/sin (``test_gpu_rope.py`` bounds those against the CPU)."""
 
 import pytest
 import torch
@@ -58,7 +59,7 @@ def test_golden_fused_prologue(golden, name):
     check(kc, ref_k, "key cache")
 
 
-def _oracle_case(config, tokens, norm, rope_kind):
+def _oracle_case(config, tokens, norm, rope_kind, variant=0):
     d = W.make_layer_inputs(config, tokens=tokens)
     shp = d["shape"]
     if rope_kind == "table":
@@ -77,21 +78,25 @@ def _oracle_case(config, tokens, norm, rope_kind):
     kc, vc = d["key_cache"].cuda(), d["value_cache"].cuda()
     normg = dict(q_weight=d["q_weight"].cuda(), k_weight=d["k_weight"].cuda(), eps=1e-6) if norm else {}
     aq, ak = ops.qk_prologue(q, k, v=v, positions=d["positions"].cuda(), **normg, **rope_g,
-                             key_cache=kc, value_cache=vc, slot_mapping=d["slot_mapping"].cuda())
+                             key_cache=kc, value_cache=vc, slot_mapping=d["slot_mapping"].cuda(),
+                             variant=variant)
     return d, (aq, ak, kc, vc), rope_o, rope_g
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("config,norm,rope_kind", [
     (1, "rms", "table"), (2, "rms", "table"), (3, "text", "interleaved"), (4, None, "chunked")])
-def test_fused_matches_composition(config, norm, rope_kind):
+def test_fused_matches_composition(config, norm, rope_kind, variant):
+    """Both kernel variants (register-staged and bulk-copy pipelined)."""
     tokens = {1: 512, 2: 256, 3: 2048, 4: 8312}[config]
-    d, (aq, ak, kc, vc), rope_o, rope_g = _oracle_case(config, tokens, norm, rope_kind)
+    d, (aq, ak, kc, vc), rope_o, rope_g = _oracle_case(config, tokens, norm, rope_kind, variant)
     shp = d["shape"]
     if rope_kind == "table":
         eq, ek, ekc, evc = O.qk_norm_rope_store(
             d["qkv"], shp.num_heads, shp.num_kv_heads, 128, positions=d["positions"], rope=rope_o,
             q_weight=d["q_weight"], k_weight=d["k_weight"], eps=1e-6, norm=norm,
-            key_cache=d["key_cache"], value_cache=d["value_cache"], slot_mapping=d["slot_mapping"])
+            key_cache=d["key_cache"], value_cache=d["value_cache"], slot_mapping=d["slot_mapping"],
+            order="kernel")
         assert_bitexact(aq, eq, "q")
         assert_bitexact(ak, ek, "k")
         assert_bitexact(kc, ekc, "key cache")
@@ -101,7 +106,8 @@ def test_fused_matches_composition(config, norm, rope_kind):
         q, k, v = d["qkv"].split([nq * 128, nkv * 128, nkv * 128], -1)
         q, k, v = q.reshape(-1, nq, 128), k.reshape(-1, nkv, 128), v.reshape(-1, nkv, 128)
         if norm == "text":
-            q, k = O.text_rms_norm(q, d["q_weight"], 1e-6), O.text_rms_norm(k, d["k_weight"], 1e-6)
+            q = O.text_rms_norm(q, d["q_weight"], 1e-6, order="kernel")
+            k = O.text_rms_norm(k, d["k_weight"], 1e-6, order="kernel")
         gc, gs = ops.mrope_cos_sin(d["positions"].cuda(), rope_g["inv_freq"], torch.bfloat16)
         eq, ek = O.apply_mrope(q, k, gc.cpu(), gs.cpu(), shp.sections, rope_kind)
         assert_bitexact(aq, eq, "q")
@@ -127,7 +133,8 @@ def test_fused_other_head_dims(head_dim):
     kc = torch.full((4, 16, nkv, head_dim), -3.0, dtype=torch.bfloat16)
     eq, ek, ekc, evc = O.qk_norm_rope_store(qkv, nq, nkv, head_dim, positions=pos, rope=("table", table),
                                             q_weight=w, k_weight=w, eps=1e-6, norm="rms",
-                                            key_cache=kc, value_cache=kc.clone(), slot_mapping=slots)
+                                            key_cache=kc, value_cache=kc.clone(), slot_mapping=slots,
+                                            order="kernel")
     gq = qkv.cuda()
     q, k, v = gq.split([nq * head_dim, nkv * head_dim, nkv * head_dim], -1)
     q, k, v = q.view(T, nq, head_dim), k.view(T, nkv, head_dim), v.view(T, nkv, head_dim)
@@ -197,3 +204,53 @@ def test_prologue_skips_minus_one_and_flags_bad_slots(monkeypatch):
         ops.qk_prologue(q, k, v=v, positions=d["positions"].cuda(), rope_mode=ops.ROPE_TABLE,
                         cos_sin_cache=table, key_cache=kc, value_cache=vc, slot_mapping=slots.cuda())
     assert bool((kc == -3).all()) and bool((vc == -3).all())
+
+
+@pytest.mark.parametrize("head_dim,heads", [(64, (8, 4)), (128, (16, 8)), (128, (16, 2)), (256, (4, 2))])
+@pytest.mark.parametrize("mode", ["table", "chunked", "interleaved", "none"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_pipelined_variant_bit_identical_to_register_variant(head_dim, heads, mode, dtype):
+    """Same inputs through variant 1 and variant 2: every output and both caches identical,
+    with and without norm / store, on a token count that is not a multiple of anything."""
+    nq, nkv = heads
+    T = 3001
+    g = torch.Generator().manual_seed(head_dim + nq)
+    qkv = torch.randn(T, (nq + 2 * nkv) * head_dim, generator=g).to(dtype).cuda()
+    q, k, v = qkv.split([nq * head_dim, nkv * head_dim, nkv * head_dim], -1)
+    q, k, v = q.view(T, nq, head_dim), k.view(T, nkv, head_dim), v.view(T, nkv, head_dim)
+    slots = torch.randperm(64 * 64, generator=g)[:T].to(torch.int32)
+    slots[::7] = -1
+    w = (1 + 0.1 * torch.randn(head_dim, generator=g)).to(dtype).cuda()
+    if mode == "table":
+        rope = dict(rope_mode=ops.ROPE_TABLE, cos_sin_cache=O.rope_cos_sin_cache(head_dim, 8192, 1e6).cuda(),
+                    positions=torch.randint(0, 8192, (T,), generator=g).cuda())
+    elif mode == "none":
+        rope = dict(rope_mode=ops.ROPE_NONE)
+    else:
+        half = head_dim // 2
+        sec = (half - 2 * (half * 5 // 16), half * 5 // 16, half * 5 // 16)
+        m = ops.ROPE_MROPE_INTERLEAVED if mode == "interleaved" else ops.ROPE_MROPE_CHUNKED
+        rope = dict(rope_mode=m, inv_freq=O.mrope_inv_freq(head_dim, 5e6).cuda(), sections=sec,
+                    positions=torch.randint(0, 32768, (3, T), generator=g).cuda())
+    for norm in (True, False):
+        for store in (True, False):
+            outs = []
+            for variant in (1, 2):
+                kc = torch.full((64, 64, nkv, head_dim), -3.0, dtype=dtype, device="cuda")
+                vc = kc.clone()
+                extra = dict(v=v, key_cache=kc, value_cache=vc, slot_mapping=slots.cuda()) if store else {}
+                nrm = dict(q_weight=w, k_weight=w, eps=1e-6) if norm else {}
+                aq, ak = ops.qk_prologue(q, k, **rope, **nrm, **extra, variant=variant)
+                outs.append((aq, ak, kc, vc))
+            for a, b, name in zip(outs[0], outs[1], ("q", "k", "key cache", "value cache")):
+                assert_bitexact(b, a, f"{name} norm={norm} store={store}")
+
+
+def test_pipelined_variant_rejects_split_layouts():
+    T = 64
+    q = torch.randn(T, 16, 128, dtype=torch.bfloat16, device="cuda")
+    k = torch.randn(T, 8, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError, match="pipelined variant"):
+        ops.qk_prologue(q, k, rope_mode=ops.ROPE_NONE, variant=2)
+    aq, ak = ops.qk_prologue(q, k, rope_mode=ops.ROPE_NONE, variant=0)  # auto: register kernel
+    assert torch.equal(aq, q) and torch.equal(ak, k)
