@@ -274,25 +274,76 @@ def launches_per_step(layers, gather_seqs):
     return 4 * layers + (2 if gather_seqs else 0)
 
 
-def run_step_e2e(inp, layers, mods, host, dev_in):
-    """One step through the layer-module API, host buffers in and out."""
+def layers_e2e(inp, layers, mods, hidden, positions, slot_mapping):
+    """The step's 28 fused layers through the layer-module API (reference-facing calls)."""
     from nano_vllm_multimodal_b200.layers.attention import attention_prologue
 
-    dev_in["hidden"].copy_(host["hidden"], non_blocking=True)
-    dev_in["positions"].copy_(host["positions"], non_blocking=True)
-    dev_in["slot_mapping"].copy_(host["slot_mapping"], non_blocking=True)
-    h, res = dev_in["hidden"], inp["residual"]
+    h, res = hidden, inp["residual"]
     h2 = None
     for _ in range(layers):
         _, h1 = mods["input_norm"](h, res)
         attention_prologue(inp["qkv"], num_heads=NQ, num_kv_heads=NKV, head_dim=D,
-                           positions=dev_in["positions"], rotary_emb=mods["rope"], q_norm=mods["q_norm"],
+                           positions=positions, rotary_emb=mods["rope"], q_norm=mods["q_norm"],
                            k_norm=mods["k_norm"], k_cache=inp["key_cache"], v_cache=inp["value_cache"],
-                           slot_mapping=dev_in["slot_mapping"])
+                           slot_mapping=slot_mapping)
         _, h2 = mods["post_norm"](inp["attn_out"], h1)
         mods["act"](inp["gate_up"])
         h, res = inp["mlp_out"], h2
-    host["out"].copy_(h2, non_blocking=True)
+    return h2
+
+
+class E2EPipeline:
+    """Steps with host inputs and host results, copies overlapped with compute.
+
+    Each step copies its inputs (initial hidden states, positions, slot mapping)
+    from pinned host memory and its final hidden states back to pinned host
+    memory. Two device input slots and two host output buffers let step k+1's
+    host->device copy (copy stream 1) and step k's device->host copy (copy
+    stream 2) run while other steps compute; events order every reuse.
+    """
+
+    KEYS = ("hidden", "positions", "slot_mapping")
+
+    def __init__(self, inp, layers, mods):
+        self.inp, self.layers, self.mods = inp, layers, mods
+        self.host_in = [{k: inp[k].cpu().pin_memory() for k in self.KEYS} for _ in range(2)]
+        self.dev_in = [{k: torch.empty_like(inp[k]) for k in self.KEYS} for _ in range(2)]
+        self.host_out = [torch.empty(inp["tokens"], H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        self.h2d, self.d2h = torch.cuda.Stream(), torch.cuda.Stream()
+        self.used = [torch.cuda.Event() for _ in range(2)]     # compute finished with dev_in[i]
+        self.ready = [torch.cuda.Event() for _ in range(2)]    # dev_in[i] filled
+
+    def bytes_per_step(self):
+        h2d = sum(t.numel() * t.element_size() for t in self.host_in[0].values())
+        return h2d, self.host_out[0].numel() * self.host_out[0].element_size()
+
+    def _load(self, slot, first):
+        if not first:
+            self.h2d.wait_event(self.used[slot])
+        with torch.cuda.stream(self.h2d):
+            for k in self.KEYS:
+                self.dev_in[slot][k].copy_(self.host_in[slot][k], non_blocking=True)
+            self.ready[slot].record(self.h2d)
+
+    def run(self, steps):
+        compute = torch.cuda.current_stream()
+        self.h2d.wait_stream(compute)
+        self.d2h.wait_stream(compute)
+        self._load(0, True)
+        for k in range(steps):
+            cur, nxt = k % 2, (k + 1) % 2
+            if k + 1 < steps:
+                self._load(nxt, k == 0)
+            compute.wait_event(self.ready[cur])
+            d = self.dev_in[cur]
+            out = layers_e2e(self.inp, self.layers, self.mods, d["hidden"], d["positions"], d["slot_mapping"])
+            self.used[cur].record(compute)
+            self.d2h.wait_event(self.used[cur])
+            with torch.cuda.stream(self.d2h):
+                self.host_out[cur].copy_(out, non_blocking=True)
+            out.record_stream(self.d2h)
+        compute.wait_stream(self.d2h)
+        compute.wait_stream(self.h2d)
 
 
 def build_modules(inp, device):
@@ -500,34 +551,27 @@ def ours_arm(args, rank, world, local):
                 "peak": hbm_peak, "unit": "GB/s", "frac": per_kernel[dom]["frac"], "traffic": traffic,
                 "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)"}
 
-    # ---- e2e through the layer API with host buffers
+    # ---- e2e through the layer API with host buffers in and out every step
     e2e = None
     if not args.no_e2e:
-        mods = build_modules(inp, device)
-        host = {"hidden": inp["hidden"].cpu().pin_memory(), "positions": inp["positions"].cpu().pin_memory(),
-                "slot_mapping": inp["slot_mapping"].cpu().pin_memory(),
-                "out": torch.empty(T, H, dtype=torch.bfloat16).pin_memory()}
-        dev_in = {"hidden": torch.empty_like(inp["hidden"]), "positions": torch.empty_like(inp["positions"]),
-                  "slot_mapping": torch.empty_like(inp["slot_mapping"])}
-        for _ in range(max(1, args.warmup)):
-            run_step_e2e(inp, args.layers, mods, host, dev_in)
+        pipe = E2EPipeline(inp, args.layers, build_modules(inp, device))
+        pipe.run(max(1, args.warmup))
         torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        for _ in range(args.steps):
-            run_step_e2e(inp, args.layers, mods, host, dev_in)
+        pipe.run(args.steps)
         e.record()
         torch.cuda.synchronize()
         barrier(world)
         e_ms = max_over_ranks(s.elapsed_time(e), world, device)
-        h2d = sum(host[k].numel() * host[k].element_size() for k in ("hidden", "positions", "slot_mapping"))
-        d2h = host["out"].numel() * host["out"].element_size()
+        h2d, d2h = pipe.bytes_per_step()
         e2e = {"value": tokens_job * args.layers * args.steps / (e_ms / 1000.0), "unit": UNIT,
                "h2d_bytes_per_step": int(max_over_ranks(float(h2d), world, device) * world),
                "d2h_bytes_per_step": int(max_over_ranks(float(d2h), world, device) * world),
-               "ms_per_step": e_ms / args.steps}
+               "ms_per_step": e_ms / args.steps,
+               "copies": "pinned host buffers, H2D and D2H on two copy streams overlapping compute"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

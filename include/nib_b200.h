@@ -137,7 +137,7 @@ typedef struct {
 /* Per token: optional per-head RMSNorm of q and k, rotary embedding of the
  * normalised q and k, rotated q/k written to q_out/k_out, and (when
  * key_cache != NULL and slot >= 0) rotated k and raw v written to the paged
- * caches. head_dim must be 64, 128 or 256 (fp32: 64 or 128). Both kernel
+ * caches. head_dim must be 64, 128 or 256. Both kernel
  * variants compute bit-identical results.
  * Replaces, fused, the sequence
  *   q_norm / k_norm        nanovllm/models/qwen3.py:82-84, qwen3_vl.py:170-171

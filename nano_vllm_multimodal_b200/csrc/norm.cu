@@ -168,12 +168,16 @@ static int launch_rms(const void* x, int64_t x_ts, int64_t x_hs, const void* res
   constexpr int E = Elem<T>::kPerVec;
   const int n = static_cast<int>(n64);
   const int nv = n / E;
-  if (nv <= 16 && !add) {
-    if (nv <= 1) launch_warp<T, W, 1, 1>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (nv <= 2) launch_warp<T, W, 2, 1>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (nv <= 4) launch_warp<T, W, 4, 1>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (nv <= 8) launch_warp<T, W, 8, 1>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else launch_warp<T, W, 16, 1>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+  if (nv <= 32 && !add) {
+    // short rows (attention heads, q/k norm): G lanes x 2 vectors, lane g owns
+    // vectors g and g + G - the rotate-half partners when a row is one head.
+    // The fused attention prologue uses the same layout and summation order.
+    const int half = (nv + 1) / 2;
+    if (half <= 1) launch_warp<T, W, 1, 2>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (half <= 2) launch_warp<T, W, 2, 2>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (half <= 4) launch_warp<T, W, 4, 2>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (half <= 8) launch_warp<T, W, 8, 2>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else launch_warp<T, W, 16, 2>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
     return launch_status("rms_norm");
   }
   if (nv <= 256) {

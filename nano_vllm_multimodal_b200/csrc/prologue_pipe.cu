@@ -19,31 +19,11 @@
 #include "bulk_copy.cuh"
 #include "dispatch.cuh"
 #include "prologue.cuh"
+#include "prologue_math.cuh"
 
 namespace nib {
 
-template <typename T> struct Packed;
-template <> struct Packed<__nv_bfloat16> {
-  using P = __nv_bfloat162;
-  __device__ __forceinline__ static P mul(P a, P b) { return __hmul2_rn(a, b); }
-  __device__ __forceinline__ static P add(P a, P b) { return __hadd2_rn(a, b); }
-  __device__ __forceinline__ static P neg(P a) { return __hneg2(a); }
-  __device__ __forceinline__ static P make(float lo, float hi) { return __floats2bfloat162_rn(lo, hi); }
-};
-template <> struct Packed<__half> {
-  using P = __half2;
-  __device__ __forceinline__ static P mul(P a, P b) { return __hmul2_rn(a, b); }
-  __device__ __forceinline__ static P add(P a, P b) { return __hadd2_rn(a, b); }
-  __device__ __forceinline__ static P neg(P a) { return __hneg2(a); }
-  __device__ __forceinline__ static P make(float lo, float hi) { return __floats2half2_rn(lo, hi); }
-};
-
-template <typename P>
-__device__ __forceinline__ uint32_t bits(P v) { return *reinterpret_cast<uint32_t*>(&v); }
-template <typename P>
-__device__ __forceinline__ P from_bits(uint32_t w) { return *reinterpret_cast<P*>(&w); }
-
-constexpr int kUG = 4;  // head groups per compute phase
+constexpr int kUG = 3;  // head groups per compute phase
 
 struct TokenMeta {
   int32_t slot;
@@ -55,13 +35,10 @@ __global__ void __launch_bounds__(kPipeMaxWarps * 32, 1)
 qk_prologue_pipe_kernel(const nib_qk_prologue_args a, const int stages, const uint32_t row_bytes,
                         const uint32_t stage_bytes) {
   constexpr int E = 8;  // 16-bit activations: 8 per 16-byte vector
-  constexpr int LPH = D / E;
-  constexpr int HPW = 32 / LPH;
-  constexpr int HALF = LPH / 2;
+  constexpr int L = D / (2 * E);  // lanes per head (paired-halves layout)
+  constexpr int HPW = 32 / L;
   constexpr int NF = D / 2;
   constexpr int FPL = (NF + 31) / 32;
-  using PK = Packed<T>;
-  using P = typename PK::P;
 
   extern __shared__ __align__(128) unsigned char smem[];
   const int lane = threadIdx.x & 31;
@@ -72,10 +49,9 @@ qk_prologue_pipe_kernel(const nib_qk_prologue_args a, const int stages, const ui
   uint64_t* bars = reinterpret_cast<uint64_t*>(tail) + wib * stages;
   float* trig = reinterpret_cast<float*>(tail + static_cast<size_t>(wpc) * stages * 8) + wib * 2 * NF;
 
-  const int hs = lane / LPH;
-  const int l = lane % LPH;
-  const bool first = l < HALF;
-  const int fb = (l % HALF) * E;
+  const int hs = lane / L;
+  const int l = lane % L;
+  const int fb = l * E;
   const int nq = a.num_heads, nkv = a.num_kv_heads;
   const bool store = a.key_cache != nullptr;
   const int Uq = (nq + HPW - 1) / HPW;
@@ -107,10 +83,10 @@ qk_prologue_pipe_kernel(const nib_qk_prologue_args a, const int stages, const ui
   __syncwarp();
 
   // ---- per-lane constants: norm weights, M-RoPE frequency layout
-  float wq[E], wk[E];
+  HeadWeights<T, W> wq, wk;
   if (a.norm) {
-    load_weights<T, W>(static_cast<const W*>(a.q_weight), l * E, wq);
-    load_weights<T, W>(static_cast<const W*>(a.k_weight), l * E, wk);
+    wq.load(static_cast<const W*>(a.q_weight), l, NF);
+    wk.load(static_cast<const W*>(a.k_weight), l, NF);
   }
   int fax[FPL];
   float finv[FPL];
@@ -120,12 +96,7 @@ qk_prologue_pipe_kernel(const nib_qk_prologue_args a, const int stages, const ui
     fax[m] = 0;
     finv[m] = 0.f;
     if (mrope && j < NF) {
-      if (inter) {
-        const int r = j % 3;
-        fax[m] = (r == 1 && j < 3 * a.sections[1]) ? 1 : (r == 2 && j < 3 * a.sections[2]) ? 2 : 0;
-      } else {
-        fax[m] = j < a.sections[0] ? 0 : (j < a.sections[0] + a.sections[1] ? 1 : 2);
-      }
+      fax[m] = mrope_axis(j, inter, a.sections);
       finv[m] = __ldg(a.inv_freq + j);
     }
   }
@@ -243,118 +214,82 @@ qk_prologue_pipe_kernel(const nib_qk_prologue_args a, const int stages, const ui
         *reinterpret_cast<float4*>(s + e) = *reinterpret_cast<const float4*>(trig + NF + fb + e);
       }
     }
-    P c2[E / 2], s2[E / 2];
-    if (inter) {
-#pragma unroll
-      for (int k = 0; k < E / 2; ++k) {
-        c2[k] = PK::make(c[2 * k], c[2 * k + 1]);  // exact: already rounded to T
-        s2[k] = PK::make(s[2 * k], s[2 * k + 1]);
-      }
-    }
+    uint32_t c2[4], s2[4];
+    if (inter) pack_trig<T>(c, s, c2, s2);
 
     // ---- q and k heads, kUG head groups per phase so that their dependency
-    // chains (squares -> butterfly -> 1/sqrt -> scale -> shuffle -> rotate)
-    // interleave instead of running back to back
-    T* qo_t = q_out + t * nq * D + hs * D + l * E;
-    T* ko_t = k_out + t * nkv * D + hs * D + l * E;
-    T* kc_t = slot >= 0 ? kc + slot * a.cache_slot_stride + hs * D + l * E : nullptr;
-    const T* rl = rq + hs * D + l * E;
+    // chains (squares -> butterfly -> 1/sqrt -> scale -> rotate) interleave
+    const int64_t qo_base = (t * nq + hs) * D + fb;
+    const int64_t ko_base = (t * nkv + hs) * D + fb;
+    T* kc_t = slot >= 0 ? kc + slot * a.cache_slot_stride + hs * D + fb : nullptr;
+    const T* rl = rq + hs * D + fb;
     const int Uqk = Uq + Uk;
     for (int u0 = 0; u0 < Uqk; u0 += kUG) {
-      uint32_t w32[kUG][4];
-      float x[kUG][E];
+      uint32_t wa[kUG][4], wb[kUG][4];
+      float xa[kUG][E], xb[kUG][E];
       bool hok[kUG], isq[kUG];
       int hoff[kUG];  // head * D within q (or within k)
 #pragma unroll
       for (int g = 0; g < kUG; ++g) {
         const int u = u0 + g;
         isq[g] = u < Uq;
-        const int hg = isq[g] ? u : u - Uq;  // head group within q or k
+        const int hg = isq[g] ? u : u - Uq;
         hoff[g] = hg * HPW * D;
         hok[g] = u < Uqk && hg * HPW + hs < (isq[g] ? nq : nkv);
-        const uint4 raw = hok[g] ? *reinterpret_cast<const uint4*>(rl + (isq[g] ? 0 : nq * D) + hoff[g])
-                                 : zero_vec();
-        w32[g][0] = raw.x; w32[g][1] = raw.y; w32[g][2] = raw.z; w32[g][3] = raw.w;
-        unpack<T>(raw, x[g]);
+        const T* src = rl + (isq[g] ? 0 : nq * D) + hoff[g];
+        const uint4 ra = hok[g] ? *reinterpret_cast<const uint4*>(src) : zero_vec();
+        const uint4 rb = hok[g] ? *reinterpret_cast<const uint4*>(src + NF) : zero_vec();
+        from_u4(ra, wa[g]);
+        from_u4(rb, wb[g]);
+        unpack<T>(ra, xa[g]);
+        unpack<T>(rb, xb[g]);
       }
       if (a.norm) {
         float ss[kUG];
 #pragma unroll
-        for (int g = 0; g < kUG; ++g) ss[g] = sumsq_tree<E>(x[g]);
+        for (int g = 0; g < kUG; ++g) ss[g] = __fadd_rn(sumsq_tree<E>(xa[g]), sumsq_tree<E>(xb[g]));
 #pragma unroll
-        for (int off = HALF; off > 0; off >>= 1) {
+        for (int off = L / 2; off > 0; off >>= 1) {
 #pragma unroll
           for (int g = 0; g < kUG; ++g) ss[g] = __fadd_rn(ss[g], __shfl_xor_sync(0xffffffffu, ss[g], off));
         }
 #pragma unroll
         for (int g = 0; g < kUG; ++g) {
           const float rs = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss[g], 1.0f / D), a.eps));
-          const float* wf = isq[g] ? wq : wk;
-#pragma unroll
-          for (int k = 0; k < E / 2; ++k) {
-            const P nn = PK::make(__fmul_rn(x[g][2 * k], rs), __fmul_rn(x[g][2 * k + 1], rs));
-            P y;
-            if constexpr (sizeof(W) == sizeof(T)) {
-              y = PK::mul(nn, PK::make(wf[2 * k], wf[2 * k + 1]));  // weights are T values: exact
-            } else {
-              y = PK::make(__fmul_rn(Elem<T>::to_f(reinterpret_cast<const T*>(&nn)[0]), wf[2 * k]),
-                           __fmul_rn(Elem<T>::to_f(reinterpret_cast<const T*>(&nn)[1]), wf[2 * k + 1]));
-            }
-            w32[g][k] = bits(y);
-          }
-          if (!inter) unpack<T>(make_uint4(w32[g][0], w32[g][1], w32[g][2], w32[g][3]), x[g]);
+          const HeadWeights<T, W>& hw = isq[g] ? wq : wk;
+          normalize_vec<T, W>(xa[g], wa[g], rs, hw.fa, hw.pa);
+          normalize_vec<T, W>(xb[g], wb[g], rs, hw.fb, hw.pb);
         }
       }
       if (mode != NIB_ROPE_NONE) {
-        uint32_t o32[kUG][4];
 #pragma unroll
-        for (int g = 0; g < kUG; ++g) {
-#pragma unroll
-          for (int k = 0; k < 4; ++k) o32[g][k] = __shfl_xor_sync(0xffffffffu, w32[g][k], HALF);
-        }
-#pragma unroll
-        for (int g = 0; g < kUG; ++g) {
-          if (inter) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const P t1 = PK::mul(from_bits<P>(w32[g][k]), c2[k]);
-              const P t2 = PK::mul(from_bits<P>(o32[g][k]), s2[k]);
-              w32[g][k] = bits(PK::add(t1, first ? PK::neg(t2) : t2));
-            }
-          } else {
-            float p[E];
-            unpack<T>(make_uint4(o32[g][0], o32[g][1], o32[g][2], o32[g][3]), p);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float a0 = __fmul_rn(x[g][2 * k], c[2 * k]), b0 = __fmul_rn(p[2 * k], s[2 * k]);
-              const float a1 = __fmul_rn(x[g][2 * k + 1], c[2 * k + 1]), b1 = __fmul_rn(p[2 * k + 1], s[2 * k + 1]);
-              w32[g][k] = bits(PK::make(first ? __fsub_rn(a0, b0) : __fadd_rn(a0, b0),
-                                        first ? __fsub_rn(a1, b1) : __fadd_rn(a1, b1)));
-            }
-          }
-        }
+        for (int g = 0; g < kUG; ++g) rotate_pair<T>(xa[g], xb[g], wa[g], wb[g], c, s, c2, s2, inter);
       }
 #pragma unroll
       for (int g = 0; g < kUG; ++g) {
         if (!hok[g]) continue;
-        const uint4 o = make_uint4(w32[g][0], w32[g][1], w32[g][2], w32[g][3]);
+        const uint4 oa = as_u4(wa[g]), ob = as_u4(wb[g]);
         if (isq[g]) {
-          st_vec(qo_t + hoff[g], o);
+          T* dst = q_out + qo_base + hoff[g];
+          st_vec(dst, oa);
+          st_vec(dst + NF, ob);
         } else {
-          st_vec(ko_t + hoff[g], o);
-          if (kc_t) st_vec(kc_t + hoff[g], o);
+          T* dst = k_out + ko_base + hoff[g];
+          st_vec(dst, oa);
+          st_vec(dst + NF, ob);
+          if (kc_t) {
+            st_vec(kc_t + hoff[g], oa);
+            st_vec(kc_t + hoff[g] + NF, ob);
+          }
         }
       }
     }
-    // ---- v heads straight from the staged row into the cache
+    // ---- v heads: the contiguous nkv*D block of the staged row into the cache slot
     if (slot >= 0) {
-      T* vc_t = vc + slot * a.cache_slot_stride + hs * D + l * E;
-      const T* rv = rl + (nq + nkv) * D;
-#pragma unroll 4
-      for (int u = 0; u < Uk; ++u) {
-        if (u * HPW + hs < nkv)
-          st_vec(vc_t + u * HPW * D, *reinterpret_cast<const uint4*>(rv + u * HPW * D));
-      }
+      T* vd = vc + slot * a.cache_slot_stride;
+      const T* vs = rq + (nq + nkv) * D;
+      for (int off = lane * E; off < nkv * D; off += 32 * E)
+        st_vec(vd + off, *reinterpret_cast<const uint4*>(vs + off));
     }
     __syncwarp();  // stage `st` and the trig scratch are rewritten next
   }

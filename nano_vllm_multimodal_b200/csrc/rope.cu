@@ -13,39 +13,40 @@
 //   store           rotated k and raw v to flat slot slot_mapping[t]
 //                   (nanovllm/layers/attention.py:87-93), -1 skipped.
 //
-// Layout: a warp owns one token; each head is covered by LPH = head_dim / 8
-// lanes holding one 16-byte vector each (bf16/fp16), so a warp processes
-// 32 / LPH heads per step. The rotate-half partner of lane l is lane l ^ LPH/2
-// (one shuffle per 32-bit word). A work item is (token, chunk of up to 8 head
-// groups); all 8 loads of an item are issued before any math. M-RoPE cos/sin
-// are computed once per item for the head_dim/2 frequencies (each lane handles
-// head_dim/64 of them) and shared through shared memory.
+// Layout (prologue_math.cuh): a head spans L = head_dim / 16 lanes (bf16/fp16;
+// head_dim / 8 for fp32), each holding a 16-byte vector of the first half and
+// its rotate-half partner vector of the second half, so a warp covers 32 / L
+// heads per step and the rotation needs no shuffles. A work item is
+// (token, chunk of up to 4 head groups); all its loads are issued before any
+// math. M-RoPE cos/sin are computed once per item for the head_dim/2
+// frequencies and shared through shared memory. This register-staged kernel
+// takes any q/k/v strides; prologue_pipe.cu is the bulk-copy variant for the
+// fused-qkv layout, with bit-identical results.
 #include "dispatch.cuh"
 #include "prologue.cuh"
+#include "prologue_math.cuh"
 
 namespace nib {
 
 constexpr int kPrologueWarps = 4;
-constexpr int kChunk = 8;
+constexpr int kChunk = 4;  // head groups per work item
 
 template <typename T, typename W, int D>
 __global__ void __launch_bounds__(kPrologueWarps * 32)
 qk_prologue_kernel(const nib_qk_prologue_args a) {
   constexpr int E = Elem<T>::kPerVec;
-  constexpr int LPH = D / E;
-  static_assert(LPH >= 2 && LPH <= 32, "head must span 2..32 lanes");
-  constexpr int HPW = 32 / LPH;
-  constexpr int HALF = LPH / 2;
+  constexpr int L = D / (2 * E);  // lanes per head (paired-halves layout)
+  static_assert(L >= 1 && L <= 32, "head must span 1..32 lanes");
+  constexpr int HPW = 32 / L;     // heads per warp step
   constexpr int NF = D / 2;
   __shared__ float s_cos[kPrologueWarps][NF];
   __shared__ float s_sin[kPrologueWarps][NF];
 
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
-  const int hs = lane / LPH;
-  const int l = lane % LPH;
-  const bool first = l < HALF;
-  const int fb = (l % HALF) * E;
+  const int hs = lane / L;
+  const int l = lane % L;
+  const int fb = l * E;
 
   const int nq = a.num_heads, nkv = a.num_kv_heads;
   const int Uq = (nq + HPW - 1) / HPW;
@@ -55,6 +56,7 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
   const int U = Uq + Uk + Uv;
   const int nchunks = (U + kChunk - 1) / kChunk;
   const int64_t items = a.tokens * nchunks;
+  const bool inter = a.rope_mode == NIB_ROPE_MROPE_INTERLEAVED;
 
   const T* q = static_cast<const T*>(a.q);
   const T* k = static_cast<const T*>(a.k);
@@ -63,8 +65,12 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
   T* k_out = static_cast<T*>(a.k_out);
   T* kc = static_cast<T*>(a.key_cache);
   T* vc = static_cast<T*>(a.value_cache);
-  const W* qw = static_cast<const W*>(a.q_weight);
-  const W* kw = static_cast<const W*>(a.k_weight);
+
+  HeadWeights<T, W> wq, wk;
+  if (a.norm) {
+    wq.load(static_cast<const W*>(a.q_weight), l, NF);
+    wk.load(static_cast<const W*>(a.k_weight), l, NF);
+  }
 
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -84,26 +90,32 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
       }
     }
 
-    // ---- issue every load of this item first
-    uint4 buf[kChunk];
+    // ---- issue every load of this item first (two vectors per lane per head)
+    uint4 ba[kChunk], bb[kChunk];
 #pragma unroll
     for (int i = 0; i < kChunk; ++i) {
       const int u = u0 + i;
-      buf[i] = zero_vec();
+      ba[i] = bb[i] = zero_vec();
+      const T* src = nullptr;
       if (u < Uq) {
         const int head = u * HPW + hs;
-        if (head < nq) buf[i] = ld_stream(q + t * a.q_token_stride + head * a.q_head_stride + l * E);
+        if (head < nq) src = q + t * a.q_token_stride + head * a.q_head_stride;
       } else if (u < Uq + Uk) {
         const int head = (u - Uq) * HPW + hs;
-        if (head < nkv) buf[i] = ld_stream(k + t * a.k_token_stride + head * a.k_head_stride + l * E);
+        if (head < nkv) src = k + t * a.k_token_stride + head * a.k_head_stride;
       } else if (u < U && slot >= 0) {
         const int head = (u - Uq - Uk) * HPW + hs;
-        if (head < nkv) buf[i] = ld_stream(v + t * a.v_token_stride + head * a.v_head_stride + l * E);
+        if (head < nkv) src = v + t * a.v_token_stride + head * a.v_head_stride;
+      }
+      if (src) {
+        ba[i] = ld_stream(src + fb);
+        bb[i] = ld_stream(src + NF + fb);
       }
     }
 
     // ---- cos / sin of this lane's E frequencies (only if the item rotates something)
     float c[E], s[E];
+    uint32_t c2[4], s2[4];
     const bool rotates = a.rope_mode != NIB_ROPE_NONE && u0 < Uq + Uk;
     if (rotates) {
       if (a.rope_mode == NIB_ROPE_TABLE) {
@@ -121,21 +133,12 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
           for (int e = 0; e < E; ++e) c[e] = s[e] = 0.f;
         }
       } else {
-        const bool inter = a.rope_mode == NIB_ROPE_MROPE_INTERLEAVED;
-        const int s0 = a.sections[0], s1 = a.sections[1], s2 = a.sections[2];
         __syncwarp();
         for (int j = lane; j < NF; j += 32) {
-          int axis;
-          if (inter) {
-            const int m = j % 3;
-            axis = (m == 1 && j < 3 * s1) ? 1 : (m == 2 && j < 3 * s2) ? 2 : 0;
-          } else {
-            axis = j < s0 ? 0 : (j < s0 + s1 ? 1 : 2);
-          }
+          const int axis = mrope_axis(j, inter, a.sections);
           const int64_t p = __ldg(a.positions + axis * a.positions_axis_stride + t * a.positions_token_stride);
-          const float f = __fmul_rn(static_cast<float>(p), __ldg(a.inv_freq + j));
           float sn, cs;
-          sincosf(f, &sn, &cs);
+          sincosf(__fmul_rn(static_cast<float>(p), __ldg(a.inv_freq + j)), &sn, &cs);
           s_cos[wib][j] = round_to<T>(cs);
           s_sin[wib][j] = round_to<T>(sn);
         }
@@ -146,6 +149,7 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
           s[e] = s_sin[wib][fb + e];
         }
       }
+      if (inter) pack_trig<T>(c, s, c2, s2);
     }
 
     // ---- per head group: norm, rotate, write
@@ -157,55 +161,40 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
         const bool is_q = u < Uq;
         const int head = is_q ? u * HPW + hs : (u - Uq) * HPW + hs;
         const bool head_ok = head < (is_q ? nq : nkv);
-        float x[E];
-        unpack<T>(buf[i], x);
+        float xa[E], xb[E];
+        uint32_t wa[4], wb[4];
+        unpack<T>(ba[i], xa);
+        unpack<T>(bb[i], xb);
+        from_u4(ba[i], wa);
+        from_u4(bb[i], wb);
         if (a.norm) {
-          float ss = sumsq_tree<E>(x);
+          float ss = __fadd_rn(sumsq_tree<E>(xa), sumsq_tree<E>(xb));
 #pragma unroll
-          for (int off = HALF; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+          for (int off = L / 2; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
           const float rs = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / D), a.eps));
-          float wf[E];
-          load_weights<T, W>(is_q ? qw : kw, l * E, wf);
-#pragma unroll
-          for (int e = 0; e < E; ++e) x[e] = round_to<T>(__fmul_rn(round_to<T>(__fmul_rn(x[e], rs)), wf[e]));
+          const HeadWeights<T, W>& hw = is_q ? wq : wk;
+          normalize_vec<T, W>(xa, wa, rs, hw.fa, hw.pa);
+          normalize_vec<T, W>(xb, wb, rs, hw.fb, hw.pb);
         }
-        if (a.rope_mode != NIB_ROPE_NONE) {
-          const uint4 mine = pack<T>(x);  // exact: x already holds T values
-          uint4 other;
-          other.x = __shfl_xor_sync(0xffffffffu, mine.x, HALF);
-          other.y = __shfl_xor_sync(0xffffffffu, mine.y, HALF);
-          other.z = __shfl_xor_sync(0xffffffffu, mine.z, HALF);
-          other.w = __shfl_xor_sync(0xffffffffu, mine.w, HALF);
-          float p[E];
-          unpack<T>(other, p);
-          if (a.rope_mode == NIB_ROPE_MROPE_INTERLEAVED) {
-#pragma unroll
-            for (int e = 0; e < E; ++e) {
-              const float t1 = round_to<T>(__fmul_rn(x[e], c[e]));
-              const float t2 = round_to<T>(__fmul_rn(p[e], s[e]));
-              x[e] = round_to<T>(first ? __fsub_rn(t1, t2) : __fadd_rn(t1, t2));
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < E; ++e) {
-              const float t1 = __fmul_rn(x[e], c[e]);
-              const float t2 = __fmul_rn(p[e], s[e]);
-              x[e] = first ? __fsub_rn(t1, t2) : __fadd_rn(t1, t2);
-            }
-          }
-        }
-        const uint4 o = pack<T>(x);
+        if (a.rope_mode != NIB_ROPE_NONE) rotate_pair<T>(xa, xb, wa, wb, c, s, c2, s2, inter);
         if (head_ok) {
-          if (is_q) {
-            st_vec(q_out + (t * nq + head) * D + l * E, o);
-          } else {
-            st_vec(k_out + (t * nkv + head) * D + l * E, o);
-            if (slot >= 0) st_vec(kc + slot * a.cache_slot_stride + head * D + l * E, o);
+          const uint4 oa = as_u4(wa), ob = as_u4(wb);
+          T* dst = is_q ? q_out + (t * nq + head) * D : k_out + (t * nkv + head) * D;
+          st_vec(dst + fb, oa);
+          st_vec(dst + NF + fb, ob);
+          if (!is_q && slot >= 0) {
+            T* cd = kc + slot * a.cache_slot_stride + head * D;
+            st_vec(cd + fb, oa);
+            st_vec(cd + NF + fb, ob);
           }
         }
       } else {
         const int head = (u - Uq - Uk) * HPW + hs;
-        if (slot >= 0 && head < nkv) st_vec(vc + slot * a.cache_slot_stride + head * D + l * E, buf[i]);
+        if (slot >= 0 && head < nkv) {
+          T* cd = vc + slot * a.cache_slot_stride + head * D;
+          st_vec(cd + fb, ba[i]);
+          st_vec(cd + NF + fb, bb[i]);
+        }
       }
     }
   }
@@ -292,9 +281,8 @@ template <typename T, typename W>
 static int launch_prologue(const nib_qk_prologue_args& a, cudaStream_t st) {
   constexpr int E = Elem<T>::kPerVec;
   const int D = a.head_dim;
-  const int lph = D / E;
+  const int lph = D / (2 * E);
   NIB_SUPPORT(D == 64 || D == 128 || D == 256, "qk_prologue: head_dim %d not supported (64/128/256)", D);
-  NIB_SUPPORT(lph <= 32, "qk_prologue: head_dim %d too large for float32 activations", D);
   const int hpw = 32 / lph;
   const int Uq = (a.num_heads + hpw - 1) / hpw;
   const int Uk = (a.num_kv_heads + hpw - 1) / hpw;
@@ -308,7 +296,7 @@ static int launch_prologue(const nib_qk_prologue_args& a, cudaStream_t st) {
   const int threads = kPrologueWarps * 32;
   if (D == 64) qk_prologue_kernel<T, W, 64><<<nb, threads, 0, st>>>(a);
   else if (D == 128) qk_prologue_kernel<T, W, 128><<<nb, threads, 0, st>>>(a);
-  else if constexpr (E == 8) qk_prologue_kernel<T, W, 256><<<nb, threads, 0, st>>>(a);
+  else qk_prologue_kernel<T, W, 256><<<nb, threads, 0, st>>>(a);
   return launch_status("qk_prologue");
 }
 

@@ -103,12 +103,12 @@ def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
 
 def prologue_supported(*tensors) -> bool:
     """Whether the fused prologue kernel takes these ``[T, heads, D]`` tensors
-    directly: head_dim 64/128/256 (fp32: 64/128), 16-byte aligned rows and
-    strides. Other layouts go through the generic rotation kernel."""
+    directly: head_dim 64/128/256, 16-byte aligned rows and strides. Other
+    layouts go through the generic rotation kernel."""
     t0 = tensors[0]
     d = t0.shape[-1]
     per_vec = 16 // t0.element_size()
-    if d not in (64, 128, 256) or (t0.dtype == torch.float32 and d == 256):
+    if d not in (64, 128, 256):
         return False
     for t in tensors:
         if t is None:

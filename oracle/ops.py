@@ -110,16 +110,19 @@ def _block_sumsq(sq, nv, vec, threads, vpt=4):
 def kernel_sumsq(s32, vec, add):
     """Sum of squares of each row of ``s32`` ([rows, n] fp32 numpy) in the
     kernels' order (``nano_vllm_multimodal_b200/csrc/norm.cu`` launch rules:
-    <= 16 vectors and no residual -> one power-of-two lane group; <= 256
-    vectors -> 32 lanes; longer rows -> one CTA, 4 vectors per thread)."""
+    <= 32 vectors and no residual -> a power-of-two group of lanes holding 2
+    vectors each (the fused attention prologue uses the same per-head layout);
+    <= 256 vectors -> 32 lanes; longer rows -> one CTA, 4 vectors per thread)."""
     rows, n = s32.shape
     nv = n // vec
     sq = (s32 * s32).astype(np.float32)
-    if nv <= 16 and not add:
+    if nv <= 32 and not add:
+        # short rows (attention heads): a lane owns vectors l and l + lanes, i.e.
+        # for a head the two rotate-half partners of the same frequencies
         lanes = 1
-        while lanes < nv:
+        while lanes < -(-nv // 2):
             lanes *= 2
-        return _lanes_sumsq(sq, nv, vec, lanes, 1)
+        return _lanes_sumsq(sq, nv, vec, lanes, 2)
     if nv <= 256:
         return _lanes_sumsq(sq, nv, vec, 32, -(-nv // 32))
     threads = -(-(-(-nv // 4)) // 32) * 32
