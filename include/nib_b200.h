@@ -198,6 +198,30 @@ NIB_API int nib_paged_gather_varlen(int dtype, const void* cache, int64_t block_
                             const int32_t* seq_lens, const int64_t* cu_seqlens, int64_t num_seqs,
                             int64_t max_seq_len, void* out, unsigned int* status, void* stream);
 
+/* Same gather as nib_paged_gather_varlen, for callers that cannot allocate
+ * device memory: hosts whose memory planner reserves the GPU up front and hands
+ * a library only the buffers it asked for, or runtimes that forbid allocation
+ * on the serving path because cudaMalloc/cudaFree synchronise the device. The
+ * per-sequence output offsets that nib_paged_gather_varlen takes from its
+ * caller (cu_seqlens) are computed here, from seq_lens, into a fixed device
+ * array that is part of this library: every GPU that loads the library holds
+ * NIB_NOALLOC_MAX_SEQS + 1 int64 offsets (32 KiB) until the process exits.
+ * No counterpart in the reference (it always has PyTorch allocate).
+ * - num_seqs above NIB_NOALLOC_MAX_SEQS is rejected with NIB_ERR_INVALID.
+ * - The first call on a device looks the array up (cudaGetSymbolAddress) with
+ *   that device current; make that first call before any stream capture.
+ * - All calls on a device share the one array and each call rewrites it:
+ *   calls whose kernels overlap on the GPU (different streams without ordering)
+ *   race on it. Order them, e.g. issue them on one stream.
+ * out receives sum(max(seq_lens[s], 0)) rows, sequence after sequence. */
+#define NIB_NOALLOC_MAX_SEQS 4096
+NIB_API int nib_paged_gather_varlen_noalloc(int dtype, const void* cache, int64_t block_stride,
+                                            int64_t slot_stride, int64_t num_blocks, int64_t block_size,
+                                            int64_t row_elems, const int32_t* block_tables,
+                                            int64_t table_stride, const int32_t* seq_lens,
+                                            int64_t num_seqs, int64_t max_seq_len, void* out,
+                                            unsigned int* status, void* stream);
+
 /* ------------------------------------------------------------------ rows */
 
 /* out[i] = weight[ids[i] - vocab_start] when vocab_start <= ids[i] < vocab_end,

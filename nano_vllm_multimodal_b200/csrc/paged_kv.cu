@@ -10,6 +10,8 @@
 // address and stride is 16-byte aligned (else 8/4/2). Out-of-range slots and
 // block ids are never dereferenced: they set a status bit (store skips the
 // token, gather writes a zero row).
+#include <mutex>
+
 #include "copy_rows.cuh"
 #include "dispatch.cuh"
 
@@ -116,6 +118,82 @@ static int gather_impl(int dtype, const void* cache, int64_t block_stride, int64
   return launch_status("paged_gather");
 }
 
+// ---------------------------------------------------------------- allocation-free variant
+// Output offsets of nib_paged_gather_varlen_noalloc: a fixed array of this
+// library's device module instead of a caller-allocated cu_seqlens buffer.
+static __device__ __align__(256) int64_t g_gather_offsets[NIB_NOALLOC_MAX_SEQS + 1];
+
+static std::mutex g_offsets_mu;
+static int64_t* g_offsets_dev[64] = {};
+
+// Device address of g_gather_offsets for the current device (looked up once
+// per device, with that device current).
+static int offsets_table(int64_t** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("paged_gather_varlen_noalloc: no usable current device (%s)", cudaGetErrorString(e));
+    return NIB_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_offsets_mu);
+  if (g_offsets_dev[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_gather_offsets);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("paged_gather_varlen_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return NIB_ERR_CUDA;
+    }
+    g_offsets_dev[dev] = static_cast<int64_t*>(p);
+  }
+  *out = g_offsets_dev[dev];
+  return NIB_OK;
+}
+
+// Exclusive prefix sums of max(lens, 0) for n <= NIB_NOALLOC_MAX_SEQS, one CTA
+// of 1024 threads with 4 entries each; writes offsets[0..n] (all of them, so
+// nothing from an earlier call is ever read).
+__global__ void __launch_bounds__(1024)
+gather_offsets_kernel(const int32_t* __restrict__ lens, int n, int64_t* __restrict__ offsets) {
+  __shared__ int64_t warp_total[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int64_t v[4], local = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = tid * 4 + k;
+    const int32_t len = i < n ? __ldg(lens + i) : 0;
+    v[k] = len > 0 ? len : 0;
+    local += v[k];
+  }
+  int64_t incl = local;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int64_t y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += y;
+  }
+  if (lane == 31) warp_total[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int64_t w = warp_total[lane];
+    int64_t wi = w;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, wi, off);
+      if (lane >= off) wi += y;
+    }
+    warp_total[lane] = wi - w;  // exclusive prefix of the warps
+  }
+  __syncthreads();
+  int64_t base = warp_total[warp] + incl - local;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = tid * 4 + k;
+    if (i < n) offsets[i] = base;
+    base += v[k];
+    if (i == n - 1) offsets[n] = base;
+  }
+  if (n == 0 && tid == 0) offsets[0] = 0;
+}
+
 }  // namespace nib
 
 using namespace nib;
@@ -182,4 +260,33 @@ extern "C" int nib_paged_gather_varlen(int dtype, const void* cache, int64_t blo
   return gather_impl(dtype, cache, block_stride, slot_stride, num_blocks, block_size, row_elems,
                      block_tables, table_stride, seq_lens, cu_seqlens, num_seqs, max_seq_len, out,
                      status, as_stream(stream));
+}
+
+extern "C" int nib_paged_gather_varlen_noalloc(int dtype, const void* cache, int64_t block_stride,
+                                               int64_t slot_stride, int64_t num_blocks,
+                                               int64_t block_size, int64_t row_elems,
+                                               const int32_t* block_tables, int64_t table_stride,
+                                               const int32_t* seq_lens, int64_t num_seqs,
+                                               int64_t max_seq_len, void* out, unsigned int* status,
+                                               void* stream) {
+  NIB_REQUIRE(num_seqs >= 0 && max_seq_len >= 0 && row_elems >= 1 && block_size >= 1,
+              "paged_gather_varlen_noalloc: bad sizes");
+  NIB_REQUIRE(num_seqs <= NIB_NOALLOC_MAX_SEQS,
+              "paged_gather_varlen_noalloc: %lld sequences exceed the fixed offset table of %d; "
+              "split the batch or use nib_paged_gather_varlen with caller-provided offsets",
+              static_cast<long long>(num_seqs), NIB_NOALLOC_MAX_SEQS);
+  if (num_seqs == 0 || max_seq_len == 0) return NIB_OK;
+  NIB_REQUIRE(cache && block_tables && seq_lens && out, "paged_gather_varlen_noalloc: null pointer");
+  NIB_REQUIRE(dtype == NIB_F32 || dtype == NIB_F16 || dtype == NIB_BF16,
+              "paged_gather_varlen_noalloc: bad dtype");
+  int64_t* offsets = nullptr;
+  int rc = offsets_table(&offsets);
+  if (rc != NIB_OK) return rc;
+  const cudaStream_t st = as_stream(stream);
+  gather_offsets_kernel<<<1, 1024, 0, st>>>(seq_lens, static_cast<int>(num_seqs), offsets);
+  rc = launch_status("paged_gather_varlen_noalloc (offsets)");
+  if (rc != NIB_OK) return rc;
+  return gather_impl(dtype, cache, block_stride, slot_stride, num_blocks, block_size, row_elems,
+                     block_tables, table_stride, seq_lens, offsets, num_seqs, max_seq_len, out, status,
+                     st);
 }
