@@ -5,9 +5,10 @@
  * Every entry point takes plain device pointers, element counts and strides
  * (in ELEMENTS, not bytes), launches on the given CUDA stream (a cudaStream_t
  * passed as void*, NULL = legacy default stream) and returns a nib_status.
- * Nothing here allocates, synchronises or reads device memory on the host,
- * so every call may be captured in a CUDA graph. On a non-zero status,
- * nib_last_error() returns a message for the calling thread.
+ * The entry points other than nib_paged_gather_varlen_noalloc neither
+ * allocate, synchronise nor read device memory on the host, so they may be
+ * captured in a CUDA graph. On a non-zero status, nib_last_error() returns a
+ * message for the calling thread.
  *
  * Index errors (slot, position, block id, token id or row out of range) never
  * cause an out-of-bounds access: the offending row is skipped or written as
