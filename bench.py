@@ -73,6 +73,7 @@ def parse_args(argv=None):
     p.add_argument("--layers", type=int, default=LAYERS)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-components", action="store_true", help="skip the per-kernel extras")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     p.add_argument("--cache-blocks", type=int, default=CACHE_BLOCKS,
                    help="blocks of 256 slots per K/V cache per GPU (smaller only for profiler captures)")
@@ -450,6 +451,75 @@ def config_block(args, world, extra=None):
     return cfg
 
 
+# ------------------------------------------------------------------ other kernels of the path
+
+
+def _time_op(fn, reps=20, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def component_bench(inp, device, hbm_peak):
+    """The path's kernels that the fused layer does not exercise on their own,
+    each at a full config size, timed with CUDA events (working sets > L2)."""
+    from nano_vllm_multimodal_b200 import ops, workloads as W
+
+    out = {}
+
+    def record(name, ms, nbytes, cfg):
+        gbs = nbytes / (ms / 1000.0) / 1e9
+        out[name] = {"avg_ms": round(ms, 4), "bytes": int(nbytes), "achieved_gbs": round(gbs, 1),
+                     "frac": round(gbs / hbm_peak, 4), "config": cfg}
+
+    T = inp["tokens"]
+    qkv = inp["qkv"]
+    q = qkv[:, : NQ * D].view(-1, NQ, D)
+    k = qkv[:, NQ * D:(NQ + NKV) * D].view(-1, NKV, D)
+    v = qkv[:, (NQ + NKV) * D:].view(-1, NKV, D)
+    ms = _time_op(lambda: ops.paged_store(k, v, inp["key_cache"], inp["value_cache"], inp["slot_mapping"]))
+    record("paged_store", ms, T * 4 * NKV * D * 2, f"C5: {T} tokens, k/v strided views of the qkv rows")
+    ms = _time_op(lambda: ops.rms_norm(q, inp["q_weight"], EPS))
+    record("rms_norm_heads", ms, T * NQ * D * 2 * 2, f"C3/C5 q-norm: [{T},{NQ},{D}] strided view")
+    # C2 embedding table (151936 x 1024 bf16), a large batch of random ids
+    seeds = W._Seeds(2, device)
+    seeds.index = 700
+    emb = W._normal(seeds, (151936, 1024), 0.0, 0.02)
+    ids = torch.randint(0, 151936, (65536,), generator=seeds(), device=device)
+    ms = _time_op(lambda: ops.embedding(ids, emb))
+    record("embedding", ms, 65536 * (4 * 1024 + 8), "C2 table 151936x1024, 65,536 random ids")
+    del emb
+    # C3 DeepStack: 16 sequences x 2048 tokens, 1024 image rows each
+    c3 = W.C3
+    hs = W._normal(seeds, (c3.tokens, c3.hidden))
+    rows = W.deepstack_rows(3, c3.tokens).to(device)
+    vis = W._normal(seeds, (rows.numel(), c3.hidden))
+    ms = _time_op(lambda: ops.deepstack_add_(hs, rows, vis))
+    record("deepstack_add_inplace", ms, rows.numel() * (6 * c3.hidden + 8),
+           "C3: hidden [32768,2048], 16,384 image rows")
+    ms = _time_op(lambda: ops.deepstack_add(hs, rows, vis))
+    record("deepstack_add_out_of_place", ms, c3.tokens * 4 * c3.hidden + rows.numel() * (6 * c3.hidden + 8),
+           "C3, copy + add")
+    del hs, vis
+    # generic M-RoPE apply on materialised cos/sin (apply_multimodal_rotary_emb)
+    pos = inp["positions"][:, :32768]
+    qq = q[:32768]
+    cos, sin = ops.mrope_cos_sin(pos, inp["inv_freq"], torch.bfloat16)
+    ms = _time_op(lambda: ops.mrope_apply(qq, cos, sin, SECTIONS, True))
+    record("mrope_apply_generic", ms, 32768 * NQ * D * 2 * 2 + 2 * 32768 * D * 2,
+           "C3 shapes, 32,768 tokens x 16 heads, cos/sin given")
+    ms = _time_op(lambda: ops.mrope_cos_sin(pos, inp["inv_freq"], torch.bfloat16))
+    record("mrope_cos_sin", ms, 3 * 32768 * 8 + 2 * 3 * 32768 * D * 2, "32,768 tokens, 3 axes")
+    return out
+
+
 # ------------------------------------------------------------------ arms
 
 
@@ -573,6 +643,10 @@ def ours_arm(args, rank, world, local):
                "ms_per_step": e_ms / args.steps,
                "copies": "pinned host buffers, H2D and D2H on two copy streams overlapping compute"}
 
+    components = None
+    if world == 1 and not args.no_components:
+        components = component_bench(inp, device, hbm_peak)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_seconds)
@@ -591,9 +665,9 @@ def ours_arm(args, rank, world, local):
         "config": config_block(args, world),
         "hbm": {"algorithmic_bytes_per_step": step_bytes_job,
                 "gbs": step_bytes_job / (ms_max / args.steps / 1000.0) / 1e9,
-                "frac_of_peak": step_bytes_job / (ms_max / args.steps / 1000.0) / 1e9 / hbm_peak,
-                "peak_gbs": hbm_peak},
-        "roofline": roofline, "kernels": per_kernel,
+                "frac_of_peak": step_bytes_job / (ms_max / args.steps / 1000.0) / 1e9 / (hbm_peak * world),
+                "peak_gbs": hbm_peak * world, "peak_note": "measured per-GPU copy bandwidth x GPUs"},
+        "roofline": roofline, "kernels": per_kernel, "components": components,
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clock,
         "gpu_launches": launches_per_step(args.layers, inp["gather_seqs"]) * args.steps,
     }

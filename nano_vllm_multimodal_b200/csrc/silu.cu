@@ -1,27 +1,60 @@
 // SiluAndMul: y = silu(x[:, :I]) * x[:, I:] (nanovllm/layers/activation.py:8-11).
 //
-// One CTA per row (grid-strided); every thread issues all of its gate/up
-// 16-byte loads for the row before any math, so a CTA keeps
-// 2 * KU * 16 B per thread in flight. The expression is evaluated in fp32 and
-// rounded once, as the reference's compiled (GPU) SiluAndMul does:
+// One CTA works on two rows at a time (rows r and r + gridDim.x of its
+// grid-strided sequence): every thread issues all of its gate/up 16-byte loads
+// for both rows before any math, so a CTA keeps 4 * KU * 16 B per thread in
+// flight. The expression is evaluated in fp32 and rounded once, as the
+// reference's compiled (GPU) SiluAndMul does:
 //   silu(g) = g / (1 + exp(-g))
-// For 2^-100 <= |g| <= 80 the exponential and the quotient use the hardware
-// approximations (ex2.approx, rcp.approx): their relative error (< 1e-5) is far
-// below half a bf16/fp16 ulp, so the rounded result stays within one ulp of
-// the exactly rounded value. Outside that range the IEEE expf / divide path
-// reproduces the reference's saturation (silu -> -0 once exp overflows).
-// float32 activations always take the IEEE path.
+// 16-bit activations: when every |g| of a 16-byte vector is <= 80, the vector
+// takes the fast form g * rcp(1 + 2^(-g*log2 e)) with the hardware ex2/rcp
+// approximations. Their arguments and results stay in the normal fp32 range
+// there, and their relative error (< 1e-5) is far below half a bf16/fp16 ulp,
+// so the rounded result stays within one ulp of the exactly rounded value.
+// Other vectors use the IEEE expf / divide form, which reproduces the
+// reference's saturation (silu -> -0 once exp overflows). float32 activations
+// always use the IEEE form.
 #include "dispatch.cuh"
 
 namespace nib {
 
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float silu_ieee(float g) { return g / (1.0f + expf(-g)); }
+
+// y[e] = round(silu(g[e]) * u[e]) for one 16-byte vector
 template <typename T>
-__device__ __forceinline__ float silu_f32(float g) {
-  // float32 outputs keep full precision: IEEE expf and divide throughout
-  if constexpr (sizeof(T) == 4) return g / (1.0f + expf(-g));
-  const float a = fabsf(g);
-  if (a <= 80.0f && a >= 0x1p-100f) return __fdividef(g, 1.0f + __expf(-g));
-  return g / (1.0f + expf(-g));  // saturating tails, tiny and subnormal inputs
+__device__ __forceinline__ uint4 silu_mul_vec(const uint4& gv, const uint4& uv) {
+  constexpr int E = Elem<T>::kPerVec;
+  float g[E], u[E], o[E];
+  unpack<T>(gv, g);
+  unpack<T>(uv, u);
+  bool fast = false;
+  if constexpr (sizeof(T) == 2) {
+    float m = fabsf(g[0]);
+#pragma unroll
+    for (int e = 1; e < E; ++e) m = fmaxf(m, fabsf(g[e]));
+    fast = m <= 80.0f;  // a NaN lane is ignored by fmax: NaN in, NaN out on either path
+  }
+  if (fast) {
+    constexpr float kNegLog2e = -1.4426950408889634f;
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+      o[e] = __fmul_rn(__fmul_rn(g[e], rcp_approx(1.0f + ex2_approx(g[e] * kNegLog2e))), u[e]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[e] = __fmul_rn(silu_ieee(g[e]), u[e]);
+  }
+  return pack<T>(o);
 }
 
 template <typename T, int KU>
@@ -29,26 +62,28 @@ __global__ void __launch_bounds__(256)
 silu_mul_rows(const T* __restrict__ x, int64_t x_rs, T* __restrict__ y, int64_t rows, int inter) {
   constexpr int E = Elem<T>::kPerVec;
   const int upr = inter / E;
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    const T* xr = x + r * x_rs;
-    uint4 g[KU], u[KU];
+  const int64_t stride = gridDim.x;
+  for (int64_t r0 = blockIdx.x; r0 < rows; r0 += 2 * stride) {
+    const int64_t r1 = r0 + stride;
+    const bool two = r1 < rows;
+    const T* x0 = x + r0 * x_rs;
+    const T* x1 = x + (two ? r1 : r0) * x_rs;
+    uint4 g0[KU], u0[KU], g1[KU], u1[KU];
 #pragma unroll
     for (int k = 0; k < KU; ++k) {
       const int j = k * blockDim.x + threadIdx.x;
       const bool ok = j < upr;
-      g[k] = ok ? ld_stream(xr + j * E) : zero_vec();
-      u[k] = ok ? ld_stream(xr + inter + j * E) : zero_vec();
+      g0[k] = ok ? ld_stream(x0 + j * E) : zero_vec();
+      u0[k] = ok ? ld_stream(x0 + inter + j * E) : zero_vec();
+      g1[k] = (ok && two) ? ld_stream(x1 + j * E) : zero_vec();
+      u1[k] = (ok && two) ? ld_stream(x1 + inter + j * E) : zero_vec();
     }
 #pragma unroll
     for (int k = 0; k < KU; ++k) {
       const int j = k * blockDim.x + threadIdx.x;
       if (j >= upr) continue;
-      float gf[E], uf[E], o[E];
-      unpack<T>(g[k], gf);
-      unpack<T>(u[k], uf);
-#pragma unroll
-      for (int e = 0; e < E; ++e) o[e] = __fmul_rn(silu_f32<T>(gf[e]), uf[e]);
-      st_vec(y + r * inter + j * E, pack<T>(o));
+      st_vec(y + r0 * inter + j * E, silu_mul_vec<T>(g0[k], u0[k]));
+      if (two) st_vec(y + r1 * inter + j * E, silu_mul_vec<T>(g1[k], u1[k]));
     }
   }
 }
@@ -66,8 +101,8 @@ static int launch_silu(const void* x, int64_t x_rs, int64_t rows, int64_t inter,
   }
   NIB_SUPPORT(ku <= 8, "silu_and_mul: intermediate size %lld is larger than this build supports",
               (long long)inter);
-  int64_t blocks = rows;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / threads) * 4;
+  int64_t blocks = (rows + 1) / 2;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / threads) * 2;
   if (blocks > cap) blocks = cap;
   const T* xp = static_cast<const T*>(x);
   T* yp = static_cast<T*>(y);

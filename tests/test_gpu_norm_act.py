@@ -125,6 +125,13 @@ def test_silu_extreme_values_and_fp32():
                          1e-30, 3.0, 80.0, 80.5, 100.0, 3e38, float("inf"), float("-inf"), -5.0,
                          -2.5, 0.5, 7.0, -1e-38])
     x = torch.cat((vals.view(1, -1), torch.full((1, vals.numel()), 1.5)), dim=1)
+    # a row whose vectors all take the fast (approximate ex2/rcp) form: edges of its range,
+    # tiny and subnormal gates
+    edge = torch.tensor([-79.9, 79.9, -1e-30, 1e-38, -3e-39, 0.0, -0.0, 1e-3,
+                         -40.0, 40.0, -1e-20, 2e-38, -7e-39, 0.25, -0.25, 60.0,
+                         -79.5, 79.5, 5e-39, -5e-39, 1.0, -1.0, 12.0, -12.0])
+    edge_row = torch.cat((edge.view(1, -1), torch.full((1, edge.numel()), -3.0)), dim=1)
+    x = torch.cat((x, edge_row), dim=0)
     for dt in (torch.bfloat16, torch.float32):
         xx = x.to(dt)
         y = ops.silu_and_mul(xx.cuda())
