@@ -18,11 +18,13 @@
 
 namespace nib {
 
-template <typename T, typename W, int G, int VPT>
+template <typename T, typename W, int G, int VPT, int RB>
 __global__ void __launch_bounds__(256)
 rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __restrict__ res,
               int64_t r_rs, const W* __restrict__ w, T* __restrict__ y, T* __restrict__ res_out,
               int64_t rows, int64_t heads, int n, float eps, int add, int round_sum) {
+  // G lanes per row, VPT 16-byte vectors per lane, RB row batches per step
+  // (all RB * VPT loads of a lane are issued before any math)
   constexpr int E = Elem<T>::kPerVec;
   constexpr int GPW = 32 / G;
   const int lane = threadIdx.x & 31;
@@ -31,54 +33,62 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int nv = n / E;
-  for (int64_t rb = warp * GPW; rb < rows; rb += nwarps * GPW) {
-    const int64_t r = rb + sub;
-    const bool active = r < rows;
-    int64_t t = 0, h = 0;
-    if (active) {
-      t = heads == 1 ? r : r / heads;
-      h = r - t * heads;
-    }
-    const T* xp = x + t * x_ts + h * x_hs;
-    const T* rp = add ? res + t * r_rs : nullptr;
-    uint4 xr[VPT], rr[VPT];
+  for (int64_t rb = warp * GPW * RB; rb < rows; rb += nwarps * GPW * RB) {
+    uint4 xr[RB][VPT], rr[RB][VPT];
+    int64_t r[RB];
+    bool active[RB];
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int vi = i * G + gl;
-      const bool ok = active && vi < nv;
-      xr[i] = ok ? ld_stream(xp + vi * E) : zero_vec();
-      rr[i] = (ok && add) ? ld_stream(rp + vi * E) : zero_vec();
-    }
-    float v[VPT][E];
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      unpack<T>(xr[i], v[i]);
-      if (add) {
-        float rv[E];
-        unpack<T>(rr[i], rv);
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const float s = __fadd_rn(v[i][e], rv[e]);
-          v[i][e] = round_sum ? round_to<T>(s) : s;
-        }
+    for (int b = 0; b < RB; ++b) {
+      r[b] = rb + b * GPW + sub;
+      active[b] = r[b] < rows;
+      int64_t t = 0, h = 0;
+      if (active[b]) {
+        t = heads == 1 ? r[b] : r[b] / heads;
+        h = r[b] - t * heads;
       }
-      ss = __fadd_rn(ss, sumsq_tree<E>(v[i]));
+      const T* xp = x + t * x_ts + h * x_hs;
+      const T* rp = add ? res + t * r_rs : nullptr;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int vi = i * G + gl;
+        const bool ok = active[b] && vi < nv;
+        xr[b][i] = ok ? ld_stream(xp + vi * E) : zero_vec();
+        rr[b][i] = (ok && add) ? ld_stream(rp + vi * E) : zero_vec();
+      }
     }
 #pragma unroll
-    for (int off = G / 2; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-    const float rs = 1.0f / sqrtf(__fadd_rn(ss / static_cast<float>(n), eps));
+    for (int b = 0; b < RB; ++b) {
+      float v[VPT][E];
+      float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int vi = i * G + gl;
-      if (!(active && vi < nv)) continue;
-      if (add) st_vec(res_out + r * n + vi * E, pack<T>(v[i]));
-      float wf[E];
-      load_weights<T, W>(w, vi * E, wf);
-      float o[E];
+      for (int i = 0; i < VPT; ++i) {
+        unpack<T>(xr[b][i], v[i]);
+        if (add) {
+          float rv[E];
+          unpack<T>(rr[b][i], rv);
 #pragma unroll
-      for (int e = 0; e < E; ++e) o[e] = __fmul_rn(round_to<T>(__fmul_rn(v[i][e], rs)), wf[e]);
-      st_vec(y + r * n + vi * E, pack<T>(o));
+          for (int e = 0; e < E; ++e) {
+            const float sv = __fadd_rn(v[i][e], rv[e]);
+            v[i][e] = round_sum ? round_to<T>(sv) : sv;
+          }
+        }
+        ss = __fadd_rn(ss, sumsq_tree<E>(v[i]));
+      }
+#pragma unroll
+      for (int off = G / 2; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+      const float rs = 1.0f / sqrtf(__fadd_rn(ss / static_cast<float>(n), eps));
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int vi = i * G + gl;
+        if (!(active[b] && vi < nv)) continue;
+        if (add) st_vec(res_out + r[b] * n + vi * E, pack<T>(v[i]));
+        float wf[E];
+        load_weights<T, W>(w, vi * E, wf);
+        float o[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[e] = __fmul_rn(round_to<T>(__fmul_rn(v[i][e], rs)), wf[e]);
+        st_vec(y + r[b] * n + vi * E, pack<T>(o));
+      }
     }
   }
 }
@@ -145,17 +155,17 @@ rms_rows_block(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __r
   }
 }
 
-template <typename T, typename W, int G, int VPT>
+template <typename T, typename W, int G, int VPT, int RB = 1>
 static void launch_warp(const void* x, int64_t x_ts, int64_t x_hs, const void* res, int64_t r_rs,
                         const void* w, void* y, void* res_out, int64_t rows, int64_t heads, int n,
                         float eps, int add, int round_sum, cudaStream_t st) {
   constexpr int kThreads = 256;
-  constexpr int rows_per_block = (kThreads / 32) * (32 / G);
+  constexpr int rows_per_block = (kThreads / 32) * (32 / G) * RB;
   int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 32;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  rms_rows_warp<T, W, G, VPT><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+  rms_rows_warp<T, W, G, VPT, RB><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
       static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
       static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
       add, round_sum);
@@ -173,11 +183,11 @@ static int launch_rms(const void* x, int64_t x_ts, int64_t x_hs, const void* res
     // vectors g and g + G - the rotate-half partners when a row is one head.
     // The fused attention prologue uses the same layout and summation order.
     const int half = (nv + 1) / 2;
-    if (half <= 1) launch_warp<T, W, 1, 2>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (half <= 2) launch_warp<T, W, 2, 2>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (half <= 4) launch_warp<T, W, 4, 2>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (half <= 8) launch_warp<T, W, 8, 2>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else launch_warp<T, W, 16, 2>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    if (half <= 1) launch_warp<T, W, 1, 2, 4>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (half <= 2) launch_warp<T, W, 2, 2, 4>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (half <= 4) launch_warp<T, W, 4, 2, 4>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (half <= 8) launch_warp<T, W, 8, 2, 4>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else launch_warp<T, W, 16, 2, 4>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
     return launch_status("rms_norm");
   }
   if (nv <= 256) {

@@ -22,6 +22,8 @@
 // frequencies and shared through shared memory. This register-staged kernel
 // takes any q/k/v strides; prologue_pipe.cu is the bulk-copy variant for the
 // fused-qkv layout, with bit-identical results.
+#include <type_traits>
+
 #include "dispatch.cuh"
 #include "prologue.cuh"
 #include "prologue_math.cuh"
@@ -247,6 +249,73 @@ mrope_apply_kernel(const TX* __restrict__ x, int64_t xts, int64_t xhs, int64_t t
   }
 }
 
+// Vectorised apply_multimodal_rotary_emb for head_dim 64/128/256 with cos/sin in
+// the activation dtype: a warp per token builds the selected cos/sin row of
+// the token in shared memory (the layout rule picks an axis per column), then
+// rotates its heads in the paired-halves layout, two 16-byte vectors per lane.
+// Same arithmetic as mrope_apply_kernel: chunked in fp32, interleaved in T
+// with every product and the sum rounded. Both halves read the selected value
+// of their own column (for interleaved the second half repeats column j).
+constexpr int kApplyWarps = 4;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kApplyWarps * 32)
+mrope_apply_vec_kernel(const T* __restrict__ x, int64_t xts, int64_t xhs, int64_t tokens, int heads,
+                       const T* __restrict__ cos, const T* __restrict__ sin, int s0, int s1, int s2,
+                       int interleaved, T* __restrict__ out) {
+  constexpr int E = Elem<T>::kPerVec;
+  constexpr int L = D / (2 * E);
+  constexpr int HPW = 32 / L;
+  constexpr int NF = D / 2;
+  __shared__ float sc[kApplyWarps][D], ss[kApplyWarps][D];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int hs = lane / L, l = lane % L, fb = l * E;
+  const int32_t sec[3] = {s0, s1, s2};
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t t = warp; t < tokens; t += nwarps) {
+    __syncwarp();
+    for (int d = lane; d < D; d += 32) {
+      const int j = d % NF;
+      const int axis = mrope_axis(j, interleaved != 0, sec);
+      const int col = interleaved ? j : d;
+      const int64_t o = (axis * tokens + t) * D + col;
+      sc[wib][d] = Elem<T>::to_f(cos[o]);
+      ss[wib][d] = Elem<T>::to_f(sin[o]);
+    }
+    __syncwarp();
+    float ca[E], cb[E], sa[E], sb[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      ca[e] = sc[wib][fb + e];
+      cb[e] = sc[wib][NF + fb + e];
+      sa[e] = ss[wib][fb + e];
+      sb[e] = ss[wib][NF + fb + e];
+    }
+    for (int h0 = 0; h0 < heads; h0 += HPW) {
+      const int h = h0 + hs;
+      if (h >= heads) continue;
+      const T* src = x + t * xts + h * xhs;
+      float xa[E], xb[E], ya[E], yb[E];
+      unpack<T>(ld_stream(src + fb), xa);
+      unpack<T>(ld_stream(src + NF + fb), xb);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        if (interleaved) {
+          ya[e] = round_to<T>(__fsub_rn(round_to<T>(__fmul_rn(xa[e], ca[e])), round_to<T>(__fmul_rn(xb[e], sa[e]))));
+          yb[e] = round_to<T>(__fadd_rn(round_to<T>(__fmul_rn(xb[e], cb[e])), round_to<T>(__fmul_rn(xa[e], sb[e]))));
+        } else {
+          ya[e] = __fsub_rn(__fmul_rn(xa[e], ca[e]), __fmul_rn(xb[e], sa[e]));
+          yb[e] = __fadd_rn(__fmul_rn(xb[e], cb[e]), __fmul_rn(xa[e], sb[e]));
+        }
+      }
+      T* dst = out + (t * heads + h) * D;
+      st_vec(dst + fb, pack<T>(ya));
+      st_vec(dst + NF + fb, pack<T>(yb));
+    }
+  }
+}
+
 template <typename TO>
 __global__ void __launch_bounds__(256)
 mrope_cos_sin_kernel(const int64_t* __restrict__ pos, int64_t pas, int64_t pts, int64_t tokens,
@@ -362,6 +431,31 @@ extern "C" int nib_mrope_apply(int x_dtype, const void* x, int64_t x_token_strid
   const cudaStream_t st = as_stream(stream);
   const unsigned grid = flat_grid(total);
   const int D = static_cast<int>(head_dim);
+  const int E = 16 / elem_size(x_dtype);
+  if (cos_dtype == x_dtype && (D == 64 || D == 128 || D == 256) && aligned16(x) && aligned16(out) &&
+      x_token_stride % E == 0 && x_head_stride % E == 0 && heads <= 65535) {
+    int64_t blocks = (tokens + kApplyWarps - 1) / kApplyWarps;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+    if (blocks > cap) blocks = cap;
+    const unsigned nb = static_cast<unsigned>(blocks);
+    const int th = kApplyWarps * 32;
+#define NIB_APPLY_VEC(TT)                                                                          \
+    do {                                                                                           \
+      auto run = [&](auto dtag) {                                                                  \
+        constexpr int DD = decltype(dtag)::value;                                                  \
+        mrope_apply_vec_kernel<TT, DD><<<nb, th, 0, st>>>(                                         \
+            static_cast<const TT*>(x), x_token_stride, x_head_stride, tokens, static_cast<int>(heads), \
+            static_cast<const TT*>(cos), static_cast<const TT*>(sin), sections[0], sections[1],   \
+            sections[2], interleaved, static_cast<TT*>(out));                                     \
+      };                                                                                           \
+      if (D == 64) run(std::integral_constant<int, 64>{});                                         \
+      else if (D == 128) run(std::integral_constant<int, 128>{});                                  \
+      else run(std::integral_constant<int, 256>{});                                                \
+    } while (0)
+    NIB_DISPATCH(x_dtype, TX, NIB_APPLY_VEC(TX));
+#undef NIB_APPLY_VEC
+    return launch_status("mrope_apply");
+  }
 #define NIB_MROPE_APPLY(TX, TC, TO)                                                              \
   mrope_apply_kernel<TX, TC, TO><<<grid, 256, 0, st>>>(                                          \
       static_cast<const TX*>(x), x_token_stride, x_head_stride, tokens, heads, D,                \
