@@ -15,6 +15,7 @@
 // written once. Rows of up to 256 vectors (2048 bf16) live in one warp's
 // registers (G lanes x VPT vectors); longer rows use one CTA per row.
 #include "dispatch.cuh"
+#include "prologue_math.cuh"
 
 namespace nib {
 
@@ -33,6 +34,20 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int nv = n / E;
+  const bool use_add = G == 32 && add != 0;  // short rows (G < 32) never carry a residual
+  // short rows: a lane's weight vectors are the same for every row - load once
+  float wfs[VPT][E];
+  uint32_t wps[VPT][4];
+  if constexpr (G < 32) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = i * G + gl;
+      if (vi < nv) {
+        load_weights<T, W>(w, vi * E, wfs[i]);
+        if constexpr (sizeof(T) == 2 && sizeof(W) == 2) from_u4(ld_vec(w + vi * E), wps[i]);
+      }
+    }
+  }
   for (int64_t rb = warp * GPW * RB; rb < rows; rb += nwarps * GPW * RB) {
     uint4 xr[RB][VPT], rr[RB][VPT];
     int64_t r[RB];
@@ -47,13 +62,13 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
         h = r[b] - t * heads;
       }
       const T* xp = x + t * x_ts + h * x_hs;
-      const T* rp = add ? res + t * r_rs : nullptr;
+      const T* rp = use_add ? res + t * r_rs : nullptr;
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int vi = i * G + gl;
         const bool ok = active[b] && vi < nv;
         xr[b][i] = ok ? ld_stream(xp + vi * E) : zero_vec();
-        rr[b][i] = (ok && add) ? ld_stream(rp + vi * E) : zero_vec();
+        rr[b][i] = (ok && use_add) ? ld_stream(rp + vi * E) : zero_vec();
       }
     }
 #pragma unroll
@@ -63,7 +78,7 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         unpack<T>(xr[b][i], v[i]);
-        if (add) {
+        if (use_add) {
           float rv[E];
           unpack<T>(rr[b][i], rv);
 #pragma unroll
@@ -81,13 +96,18 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
       for (int i = 0; i < VPT; ++i) {
         const int vi = i * G + gl;
         if (!(active[b] && vi < nv)) continue;
-        if (add) st_vec(res_out + r[b] * n + vi * E, pack<T>(v[i]));
-        float wf[E];
-        load_weights<T, W>(w, vi * E, wf);
-        float o[E];
-#pragma unroll
-        for (int e = 0; e < E; ++e) o[e] = __fmul_rn(round_to<T>(__fmul_rn(v[i][e], rs)), wf[e]);
-        st_vec(y + r[b] * n + vi * E, pack<T>(o));
+        if (use_add) st_vec(res_out + r[b] * n + vi * E, pack<T>(v[i]));
+        uint32_t words[4];
+        if constexpr (G < 32) {
+          normalize_vec<T, W>(v[i], words, rs, wfs[i], wps[i]);
+        } else {
+          float wf[E];
+          uint32_t wp[4];
+          load_weights<T, W>(w, vi * E, wf);
+          if constexpr (sizeof(T) == 2 && sizeof(W) == 2) from_u4(ld_vec(w + vi * E), wp);
+          normalize_vec<T, W>(v[i], words, rs, wf, wp);
+        }
+        st_vec(y + r[b] * n + vi * E, as_u4(words));
       }
     }
   }
@@ -146,11 +166,11 @@ rms_rows_block(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __r
       if (vi >= nv) continue;
       if (add) st_vec(res_out + r * n + vi * E, pack<T>(v[i]));
       float wf[E];
+      uint32_t wp[4], words[4];
       load_weights<T, W>(w, vi * E, wf);
-      float o[E];
-#pragma unroll
-      for (int e = 0; e < E; ++e) o[e] = __fmul_rn(round_to<T>(__fmul_rn(v[i][e], rs)), wf[e]);
-      st_vec(y + r * n + vi * E, pack<T>(o));
+      if constexpr (sizeof(T) == 2 && sizeof(W) == 2) from_u4(ld_vec(w + vi * E), wp);
+      normalize_vec<T, W>(v[i], words, rs, wf, wp);
+      st_vec(y + r * n + vi * E, as_u4(words));
     }
   }
 }
@@ -183,11 +203,11 @@ static int launch_rms(const void* x, int64_t x_ts, int64_t x_hs, const void* res
     // vectors g and g + G - the rotate-half partners when a row is one head.
     // The fused attention prologue uses the same layout and summation order.
     const int half = (nv + 1) / 2;
-    if (half <= 1) launch_warp<T, W, 1, 2, 4>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (half <= 2) launch_warp<T, W, 2, 2, 4>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (half <= 4) launch_warp<T, W, 4, 2, 4>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (half <= 8) launch_warp<T, W, 8, 2, 4>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else launch_warp<T, W, 16, 2, 4>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    if (half <= 1) launch_warp<T, W, 1, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (half <= 2) launch_warp<T, W, 2, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (half <= 4) launch_warp<T, W, 4, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else if (half <= 8) launch_warp<T, W, 8, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    else launch_warp<T, W, 16, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
     return launch_status("rms_norm");
   }
   if (nv <= 256) {
