@@ -526,7 +526,63 @@ def component_bench(inp, device, hbm_peak):
     record("mrope_cos_sin", ms, 3 * 32768 * 8 + 2 * 3 * 32768 * D * 2,
            "32,768 tokens, 3 axes (sincosf-bound: 6.3 M sincos per call)")
     del flush
+    out["c2_decode_layer_graph"] = decode_layer_graph(device)
     return out
+
+
+def decode_layer_graph(device, layers=28, replays=50):
+    """C2 decode step (Qwen3-0.6B shapes, 256 tokens, 10% padded slots): the
+    fused elementwise layer x28 captured once in a CUDA graph and replayed.
+    Small batches are launch-bound, not HBM-bound: reported as time per layer."""
+    from nano_vllm_multimodal_b200 import ops, workloads as W
+
+    d = W.make_layer_inputs(2, device=device)
+    shp = d["shape"]
+    nq, nkv, hd = shp.num_heads, shp.num_kv_heads, shp.head_dim
+    from nano_vllm_multimodal_b200.layers.rotary_embedding import RotaryEmbedding
+
+    table = RotaryEmbedding(hd, hd, shp.max_position, shp.theta).to(device).cos_sin_cache
+    qkv = d["qkv"]
+    q, k, v = qkv.split([nq * hd, nkv * hd, nkv * hd], -1)
+    q, k, v = q.view(-1, nq, hd), k.view(-1, nkv, hd), v.view(-1, nkv, hd)
+
+    def step():
+        h, res = d["hidden"], d["residual"]
+        for _ in range(layers):
+            _, h1 = ops.add_rms_norm(h, res, d["w_in"], 1e-6)
+            ops.qk_prologue(q, k, v=v, positions=d["positions"], q_weight=d["q_weight"], k_weight=d["k_weight"],
+                            eps=1e-6, rope_mode=ops.ROPE_TABLE, cos_sin_cache=table, key_cache=d["key_cache"],
+                            value_cache=d["value_cache"], slot_mapping=d["slot_mapping"])
+            _, h2 = ops.add_rms_norm(d["attn_out"], h1, d["w_post"], 1e-6)
+            ops.silu_and_mul(d["gate_up"])
+            h, res = d["hidden"], h2
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us_layer = e0.elapsed_time(e1) * 1000.0 / (replays * layers)
+    del graph
+    return {"us_per_layer": round(us_layer, 2), "launches_per_layer": 4,
+            "tokens": shp.tokens, "layers_per_graph": layers,
+            "bytes_per_layer": shp.tokens * (2 * 8 * shp.hidden + 2 * ((nq + 2 * nkv) * hd + nq * hd + nkv * hd
+                                                                        + 2 * nkv * hd) + 12 + 6 * shp.intermediate),
+            "config": "C2 decode: 256 tokens, hidden 1024, 16/8 heads, 1-D RoPE (theta 1e6), 10% slots -1, "
+                      "I=3072; 28 layers per captured graph"}
 
 
 # ------------------------------------------------------------------ arms
