@@ -23,6 +23,9 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // number of SMs of the current device (cached per device)
 int sm_count();
 
+// Largest grid.x a one-shot launch uses; kernels grid-stride past it.
+constexpr int64_t kMaxGrid = 0x7fffffff;
+
 #define NIB_REQUIRE(cond, ...)                 \
   do {                                         \
     if (!(cond)) {                             \
@@ -70,9 +73,15 @@ __device__ __forceinline__ float round_to(float v) {
 __device__ __forceinline__ uint4 ld_vec(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
-// read-once streaming input: evict-first in L1/L2
+// read-once streaming input: no L1 allocation, L2 fetches whole 256-byte
+// blocks (the neighbouring 16-byte vectors of the row are read next). A
+// coherent load: in-place callers write the same rows after reading them.
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
-  return __ldcs(reinterpret_cast<const uint4*>(p));
+  uint4 v;
+  asm volatile("ld.global.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
 }
 __device__ __forceinline__ void st_vec(void* p, const uint4& v) {
   *reinterpret_cast<uint4*>(p) = v;

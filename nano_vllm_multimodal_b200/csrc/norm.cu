@@ -182,7 +182,10 @@ static void launch_warp(const void* x, int64_t x_ts, int64_t x_hs, const void* r
   constexpr int kThreads = 256;
   constexpr int rows_per_block = (kThreads / 32) * (32 / G) * RB;
   int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * 32;
+  // Full-warp rows: one-shot CTAs (a retiring CTA's store drain overlaps the
+  // next CTA's loads; measured 3% faster on B200 than 32 persistent CTAs per
+  // SM). Short rows keep persistent warps, which load their weights once.
+  const int64_t cap = G < 32 ? static_cast<int64_t>(sm_count()) * 32 : kMaxGrid;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   rms_rows_warp<T, W, G, VPT, RB><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(

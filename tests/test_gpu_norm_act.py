@@ -120,6 +120,22 @@ def test_silu_configs(config, dtype):
     assert int((d2 > 1).sum()) <= max(3, int(1e-5 * d2.numel()))
 
 
+@pytest.mark.parametrize("rows,inter", [(1023, 512), (13, 136), (5, 16384), (7, 2056), (1, 8), (3, 1000)])
+def test_silu_row_shapes(rows, inter):
+    """CTA shapes: several rows per CTA with a ragged last CTA (short rows), up to 8
+    vectors per thread (long rows), partial last vector group."""
+    g = torch.Generator().manual_seed(rows * 7 + inter)
+    x = torch.randn(rows, 2 * inter, generator=g).to(torch.bfloat16)
+    y = ops.silu_and_mul(x.cuda())
+    assert_ulp(y, O.silu_and_mul_fp32(x), 1, f"silu rows={rows} inter={inter}")
+
+
+def test_silu_rejects_rows_longer_than_supported():
+    x = torch.zeros(2, 2 * 16392, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError, match="larger than this build supports"):
+        ops.silu_and_mul(x)
+
+
 def test_silu_extreme_values_and_fp32():
     vals = torch.tensor([-200.0, -100.0, -88.9, -88.5, -87.5, -80.5, -80.0, -20.0, -1e-3, 0.0, -0.0,
                          1e-30, 3.0, 80.0, 80.5, 100.0, 3e38, float("inf"), float("-inf"), -5.0,
