@@ -31,7 +31,7 @@ struct TokenMeta {
 };
 
 template <typename T, typename W, int D>
-__global__ void __launch_bounds__(kPipeMaxWarps * 32, 1)
+__global__ void __launch_bounds__(pipe_max_warps<W>() * 32, 1)
 qk_prologue_pipe_kernel(const nib_qk_prologue_args a, const int stages, const uint32_t row_bytes,
                         const uint32_t stage_bytes) {
   constexpr int E = 8;  // 16-bit activations: 8 per 16-byte vector
@@ -307,8 +307,9 @@ static bool pipe_layout(const nib_qk_prologue_args& a, PipeLayout* out) {
   const uint32_t stage_bytes = (row_bytes + tab + 127u) / 128u * 128u;
   const uint32_t trig = (a.rope_mode == NIB_ROPE_MROPE_CHUNKED || a.rope_mode == NIB_ROPE_MROPE_INTERLEAVED)
                             ? D * 4 : 0;  // 2 * (D/2) floats
-  for (int stages = kPipeStages; stages >= 2; --stages) {
-    for (int warps = kPipeMaxWarps; warps >= 2; warps -= 2) {
+  const bool fp32_weights = a.norm && a.weight_dtype == NIB_F32;
+  for (int stages = pipe_max_stages(fp32_weights); stages >= 2; --stages) {
+    for (int warps = pipe_max_warps(fp32_weights); warps >= 2; warps -= 2) {
       const uint32_t bytes = warps * (stages * stage_bytes + stages * 8 + trig);
       if (bytes <= kPipeSmemBudget) {
         *out = PipeLayout{warps, stages, row_bytes, stage_bytes, bytes};
