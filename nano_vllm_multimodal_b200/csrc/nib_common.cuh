@@ -63,6 +63,21 @@ template <> struct Elem<__half> {
   __device__ __forceinline__ static __half from_f(float v) { return __float2half_rn(v); }
 };
 
+// two adjacent elements rounded from fp32 (round to nearest each), one store
+template <typename T> struct Vec2;
+template <> struct Vec2<float> {
+  using type = float2;
+  __device__ __forceinline__ static float2 make(float a, float b) { return make_float2(a, b); }
+};
+template <> struct Vec2<__nv_bfloat16> {
+  using type = __nv_bfloat162;
+  __device__ __forceinline__ static __nv_bfloat162 make(float a, float b) { return __floats2bfloat162_rn(a, b); }
+};
+template <> struct Vec2<__half> {
+  using type = __half2;
+  __device__ __forceinline__ static __half2 make(float a, float b) { return __floats2half2_rn(a, b); }
+};
+
 // round an fp32 value to T and back (identity for float)
 template <typename T>
 __device__ __forceinline__ float round_to(float v) {

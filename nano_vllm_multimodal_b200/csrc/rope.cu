@@ -274,6 +274,14 @@ mrope_apply_vec_kernel(const T* __restrict__ x, int64_t xts, int64_t xhs, int64_
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   for (int64_t t = warp; t < tokens; t += nwarps) {
+    // the first head group's vectors are loaded before the cos/sin selection,
+    // and every group prefetches the next one's before its own math
+    uint4 na = zero_vec(), nb = zero_vec();
+    if (hs < heads) {
+      const T* src = x + t * xts + static_cast<int64_t>(hs) * xhs;
+      na = ld_stream(src + fb);
+      nb = ld_stream(src + NF + fb);
+    }
     __syncwarp();
     for (int d = lane; d < D; d += 32) {
       const int j = d % NF;
@@ -294,11 +302,16 @@ mrope_apply_vec_kernel(const T* __restrict__ x, int64_t xts, int64_t xhs, int64_
     }
     for (int h0 = 0; h0 < heads; h0 += HPW) {
       const int h = h0 + hs;
+      const uint4 va = na, vb = nb;
+      if (h + HPW < heads) {
+        const T* src = x + t * xts + static_cast<int64_t>(h + HPW) * xhs;
+        na = ld_stream(src + fb);
+        nb = ld_stream(src + NF + fb);
+      }
       if (h >= heads) continue;
-      const T* src = x + t * xts + h * xhs;
       float xa[E], xb[E], ya[E], yb[E];
-      unpack<T>(ld_stream(src + fb), xa);
-      unpack<T>(ld_stream(src + NF + fb), xb);
+      unpack<T>(va, xa);
+      unpack<T>(vb, xb);
 #pragma unroll
       for (int e = 0; e < E; ++e) {
         if (interleaved) {
@@ -318,7 +331,7 @@ mrope_apply_vec_kernel(const T* __restrict__ x, int64_t xts, int64_t xhs, int64_
 
 template <typename TO>
 __global__ void __launch_bounds__(256)
-mrope_cos_sin_kernel(const int64_t* __restrict__ pos, int64_t pas, int64_t pts, int64_t tokens,
+mrope_cos_sin_any_kernel(const int64_t* __restrict__ pos, int64_t pas, int64_t pts, int64_t tokens,
                      const float* __restrict__ inv_freq, int D, TO* __restrict__ cos,
                      TO* __restrict__ sin) {
   const int half = D / 2;
@@ -335,6 +348,49 @@ mrope_cos_sin_kernel(const int64_t* __restrict__ pos, int64_t pas, int64_t pts, 
     const int64_t o = (ax * tokens + t) * D + j;
     cos[o] = cos[o + half] = Elem<TO>::from_f(cs);
     sin[o] = sin[o + half] = Elem<TO>::from_f(sn);
+  }
+}
+
+// Even half-widths: a thread computes frequencies j and j+1 of kCosSinTok
+// consecutive tokens and writes each of cos/sin as packed 2-element stores into
+// the first and second half of head_dim; the axis is blockIdx.y. HP = pairs per
+// token when it is a compile-time constant (head_dim 64/128/256), else 0.
+// All position loads are issued before the 2*kCosSinTok independent sincosf.
+constexpr int kCosSinTok = 4;
+template <typename TO, int HP>
+__global__ void __launch_bounds__(256)
+mrope_cos_sin_pair_kernel(const int64_t* __restrict__ pos, int64_t pas, int64_t pts, int64_t tokens,
+                          const float* __restrict__ inv_freq, int D, TO* __restrict__ cos,
+                          TO* __restrict__ sin) {
+  using P2 = typename Vec2<TO>::type;
+  const int half = D / 2;
+  const int hp = HP > 0 ? HP : half / 2;
+  const int64_t ax = blockIdx.y;
+  const int64_t groups = (tokens + kCosSinTok - 1) / kCosSinTok;
+  const int64_t total = groups * hp;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t tg = idx / hp;
+    const int j = 2 * static_cast<int>(idx - tg * hp);
+    const int64_t t0 = tg * kCosSinTok;
+    const float f0 = __ldg(inv_freq + j), f1 = __ldg(inv_freq + j + 1);
+    float p[kCosSinTok];
+#pragma unroll
+    for (int k = 0; k < kCosSinTok; ++k)
+      p[k] = t0 + k < tokens ? static_cast<float>(__ldg(pos + ax * pas + (t0 + k) * pts)) : 0.f;
+#pragma unroll
+    for (int k = 0; k < kCosSinTok; ++k) {
+      if (t0 + k >= tokens) break;
+      float s0, c0, s1, c1;
+      sincosf(__fmul_rn(p[k], f0), &s0, &c0);
+      sincosf(__fmul_rn(p[k], f1), &s1, &c1);
+      const int64_t o = (ax * tokens + t0 + k) * D + j;
+      const P2 cv = Vec2<TO>::make(c0, c1), sv = Vec2<TO>::make(s0, s1);
+      *reinterpret_cast<P2*>(cos + o) = cv;
+      *reinterpret_cast<P2*>(cos + o + half) = cv;
+      *reinterpret_cast<P2*>(sin + o) = sv;
+      *reinterpret_cast<P2*>(sin + o + half) = sv;
+    }
   }
 }
 
@@ -489,10 +545,35 @@ extern "C" int nib_mrope_cos_sin(const int64_t* positions, int64_t positions_axi
   if (tokens == 0) return NIB_OK;
   NIB_REQUIRE(positions && inv_freq && cos && sin, "mrope_cos_sin: null pointer");
   const cudaStream_t st = as_stream(stream);
+  const int D = static_cast<int>(head_dim);
+  const int es = elem_size(out_dtype);
+  if ((D / 2) % 2 == 0 && reinterpret_cast<uintptr_t>(cos) % (2 * es) == 0 &&
+      reinterpret_cast<uintptr_t>(sin) % (2 * es) == 0) {
+    // one-shot grid, axis on y
+    int64_t blocks = ((tokens + kCosSinTok - 1) / kCosSinTok * (D / 4) + 255) / 256;
+    if (blocks > kMaxGrid) blocks = kMaxGrid;
+    const dim3 grid(static_cast<unsigned>(blocks), 3);
+#define NIB_COS_SIN_PAIR(HP)                                                                    \
+  NIB_DISPATCH(out_dtype, TO,                                                                   \
+               mrope_cos_sin_pair_kernel<TO, HP><<<grid, 256, 0, st>>>(                         \
+                   positions, positions_axis_stride, positions_token_stride, tokens, inv_freq, D, \
+                   static_cast<TO*>(cos), static_cast<TO*>(sin)))
+    if (D == 64) {
+      NIB_COS_SIN_PAIR(16);
+    } else if (D == 128) {
+      NIB_COS_SIN_PAIR(32);
+    } else if (D == 256) {
+      NIB_COS_SIN_PAIR(64);
+    } else {
+      NIB_COS_SIN_PAIR(0);
+    }
+#undef NIB_COS_SIN_PAIR
+    return launch_status("mrope_cos_sin");
+  }
   const unsigned grid = flat_grid(3 * tokens * (head_dim / 2), 16);
   NIB_DISPATCH(out_dtype, TO,
-               mrope_cos_sin_kernel<TO><<<grid, 256, 0, st>>>(
-                   positions, positions_axis_stride, positions_token_stride, tokens, inv_freq,
-                   static_cast<int>(head_dim), static_cast<TO*>(cos), static_cast<TO*>(sin)));
+               mrope_cos_sin_any_kernel<TO><<<grid, 256, 0, st>>>(
+                   positions, positions_axis_stride, positions_token_stride, tokens, inv_freq, D,
+                   static_cast<TO*>(cos), static_cast<TO*>(sin)));
   return launch_status("mrope_cos_sin");
 }

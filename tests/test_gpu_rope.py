@@ -161,6 +161,23 @@ def test_generic_apply_matches_oracle(strategy, dtype):
         assert_bitexact(ak, ek, f"k {D} {dtype}")
 
 
+@pytest.mark.parametrize("D", [64, 128, 256, 12, 6, 2])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_mrope_cos_sin_head_dims_and_dtypes(D, dtype):
+    """Paired-frequency kernel (even D/2; compile-time pairs for 64/128/256) and the
+    per-element kernel (odd D/2) against torch's CUDA cos/sin, bit-exact; positions
+    read through a token stride of 2 and a token count that leaves partial CTAs."""
+    g = torch.Generator().manual_seed(D)
+    T = 1001  # not a multiple of the 4 tokens per thread
+    pos = torch.randint(0, 40000, (3, 2 * T), generator=g).cuda()[:, ::2]
+    inv = (1.0 / (5e6 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).cuda()
+    c, s = ops.mrope_cos_sin(pos, inv, dtype)
+    f = pos.float().unsqueeze(-1) * inv.view(1, 1, -1)
+    emb = torch.cat((f, f), -1)
+    assert_bitexact(c, emb.cos().to(dtype), f"cos D={D} {dtype}")
+    assert_bitexact(s, emb.sin().to(dtype), f"sin D={D} {dtype}")
+
+
 def test_module_forward_and_cos_sin():
     d = W.make_layer_inputs(3, tokens=512, cache=False)
     mod = MultimodalRotaryEmbedding(head_dim=128, base=5e6, sections=(24, 20, 20),
