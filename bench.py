@@ -514,7 +514,23 @@ def component_bench(inp, device, hbm_peak):
     ms = _time_op(flush=flush, fn=lambda: ops.deepstack_add(hs, rows, vis))
     record("deepstack_add_out_of_place", ms, c3.tokens * 4 * c3.hidden + rows.numel() * (6 * c3.hidden + 8),
            "C3, copy + add")
-    del hs, vis
+    # Qwen3-VL layer boundary with DeepStack folded in: rounded add + visual-row add + text norm
+    res = W._normal(seeds, (c3.tokens, c3.hidden))
+    wn = W._normal(seeds, (c3.hidden,), 1.0, 0.1)
+    ridx = ops.deepstack_row_index(rows, c3.tokens)
+    ms = _time_op(flush=flush, fn=lambda: ops.add_rms_norm_deepstack(hs, res, wn, EPS, vis, ridx))
+
+    def unfused():
+        s = hs + res
+        ops.deepstack_add_(s, rows, vis)
+        return ops.rms_norm(s, wn, EPS)
+
+    ms_unfused = _time_op(flush=flush, fn=unfused)
+    record("add_norm_deepstack", ms, c3.tokens * (8 * c3.hidden + 4) + rows.numel() * 2 * c3.hidden,
+           "C3: [32768,2048] + 16,384 visual rows, one pass")
+    out["add_norm_deepstack"]["unfused_ms"] = round(ms_unfused, 4)
+    out["add_norm_deepstack"]["unfused"] = "torch add + deepstack_add_ + rms_norm"
+    del hs, vis, res
     # generic M-RoPE apply on materialised cos/sin (apply_multimodal_rotary_emb)
     pos = inp["positions"][:, :32768]
     qq = q[:32768]

@@ -80,6 +80,24 @@ NIB_API int nib_add_rms_norm(int dtype, const void* x, int64_t x_row_stride, con
                      const void* weight, float eps, int round_sum, void* out, void* residual_out,
                      void* stream);
 
+/* Qwen3-VL layer boundary with the DeepStack add folded in (one token per row):
+ *   s = dtype(x + residual); if index[t] >= 0: s = dtype(s + vis[index[t]]);
+ *   out = Qwen3VLTextRMSNorm(s); residual_out = s
+ * in one pass over [rows, n]. index is int32 [rows] (nib_deepstack_row_index);
+ * vis is [vis_rows, n] with row stride vis_row_stride. An index outside
+ * [-1, vis_rows) sets NIB_DEV_BAD_INDEX in *status (when given) and the token
+ * is treated as text. out/residual_out may alias x or residual as in
+ * nib_add_rms_norm; vis must not alias them.
+ * Replaces, in one kernel: the layer output add (nanovllm/models/qwen3_vl.py:238),
+ * _add_deepstack_rows (qwen3_vl.py:332-344, called at :371-376) and the next
+ * layer's input add + input_layernorm (qwen3_vl.py:232-235, 74-79). */
+NIB_API int nib_add_rms_norm_deepstack(int dtype, const void* x, int64_t x_row_stride,
+                               const void* residual, int64_t residual_row_stride, int64_t rows,
+                               int64_t n, int weight_dtype, const void* weight, float eps,
+                               const void* vis, int64_t vis_row_stride, int64_t vis_rows,
+                               const int32_t* index, void* out, void* residual_out,
+                               unsigned int* status, void* stream);
+
 /* ------------------------------------------------------------------ activation */
 
 /* y[t, :] = silu(x[t, :I]) * x[t, I:2I], computed in fp32, rounded once.
@@ -242,6 +260,17 @@ NIB_API int nib_embedding(int dtype, const int64_t* ids, int64_t n_ids, const vo
 NIB_API int nib_deepstack_add(int dtype, void* hidden, int64_t hidden_row_stride, int64_t tokens,
                       int64_t n, const int64_t* rows, int64_t n_rows, const void* vis,
                       int64_t vis_row_stride, unsigned int* status, void* stream);
+
+/* index[t] = j for t = rows[j] (j < n_rows), -1 for every other t < tokens:
+ * the token -> visual-row map nib_add_rms_norm_deepstack reads. rows are the
+ * sorted distinct visual token rows of _add_deepstack_rows; a row outside
+ * [0, tokens) sets NIB_DEV_BAD_INDEX in *status (when given) and is skipped.
+ * Two launches (fill, scatter) on `stream`; no allocation, no synchronisation.
+ * Replaces: the row selection of _add_deepstack_rows
+ * nanovllm/models/qwen3_vl.py:332-344 (built once per forward, used by the
+ * three DeepStack layers) */
+NIB_API int nib_deepstack_row_index(const int64_t* rows, int64_t n_rows, int64_t tokens,
+                            int32_t* index, unsigned int* status, void* stream);
 
 /* out[r] = in[r] for r < rows (n elements per row): the out-of-place half of
  * _add_deepstack_rows (the clone at nanovllm/models/qwen3_vl.py:342). */

@@ -11,6 +11,12 @@
 // fixed (sumsq_tree per 16-byte vector, vectors in order per lane, lanes by
 // xor butterfly, warps in order); PyTorch leaves its order unspecified.
 //
+// DeepStack fold (Qwen3-VL, DS = true, rounded-sum add only): a token t with
+// index[t] = j >= 0 adds visual row j after the residual add and before the
+// statistics, s = dtype(dtype(x + residual) + vis[j]), which is the order of
+// the reference's layer output add (qwen3_vl.py:238), _add_deepstack_rows
+// (qwen3_vl.py:332-344, called at :371-376) and the next input_layernorm.
+//
 // Layout: rows of n elements, each row read once with 16-byte vectors and
 // written once. Rows of up to 256 vectors (2048 bf16) live in one warp's
 // registers (G lanes x VPT vectors); longer rows use one CTA per row.
@@ -19,11 +25,30 @@
 
 namespace nib {
 
-template <typename T, typename W, int G, int VPT, int RB>
+// DeepStack operands of the folded kernels (unused when DS = false)
+struct DsArgs {
+  const void* vis = nullptr;       // [vis_rows, n] visual embeddings
+  int64_t vis_rs = 0;              // row stride in elements
+  int64_t vis_rows = 0;
+  const int32_t* index = nullptr;  // [rows]: visual row of each token or -1
+  unsigned int* status = nullptr;
+};
+
+// visual row of token t (-1: none); an index outside [-1, vis_rows) is reported and ignored
+__device__ __forceinline__ int64_t ds_row(const DsArgs& ds, int64_t t) {
+  const int64_t j = __ldg(ds.index + t);
+  if (j >= ds.vis_rows || j < -1) {
+    flag(ds.status, NIB_DEV_BAD_INDEX);
+    return -1;
+  }
+  return j;
+}
+
+template <typename T, typename W, int G, int VPT, int RB, bool DS = false>
 __global__ void __launch_bounds__(256)
 rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __restrict__ res,
               int64_t r_rs, const W* __restrict__ w, T* __restrict__ y, T* __restrict__ res_out,
-              int64_t rows, int64_t heads, int n, float eps, int add, int round_sum) {
+              int64_t rows, int64_t heads, int n, float eps, int add, int round_sum, DsArgs ds) {
   // G lanes per row, VPT 16-byte vectors per lane, RB row batches per step
   // (all RB * VPT loads of a lane are issued before any math)
   constexpr int E = Elem<T>::kPerVec;
@@ -49,8 +74,8 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
     }
   }
   for (int64_t rb = warp * GPW * RB; rb < rows; rb += nwarps * GPW * RB) {
-    uint4 xr[RB][VPT], rr[RB][VPT];
-    int64_t r[RB];
+    uint4 xr[RB][VPT], rr[RB][VPT], dr[RB][DS ? VPT : 1];
+    int64_t r[RB], dj[RB];
     bool active[RB];
 #pragma unroll
     for (int b = 0; b < RB; ++b) {
@@ -61,6 +86,7 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
         t = heads == 1 ? r[b] : r[b] / heads;
         h = r[b] - t * heads;
       }
+      if constexpr (DS) dj[b] = active[b] ? ds_row(ds, t) : -1;  // heads == 1
       const T* xp = x + t * x_ts + h * x_hs;
       const T* rp = use_add ? res + t * r_rs : nullptr;
 #pragma unroll
@@ -69,6 +95,14 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
         const bool ok = active[b] && vi < nv;
         xr[b][i] = ok ? ld_stream(xp + vi * E) : zero_vec();
         rr[b][i] = (ok && use_add) ? ld_stream(rp + vi * E) : zero_vec();
+      }
+      if constexpr (DS) {
+        const T* vp = static_cast<const T*>(ds.vis) + (dj[b] >= 0 ? dj[b] : 0) * ds.vis_rs;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+          const int vi = i * G + gl;
+          dr[b][i] = (dj[b] >= 0 && vi < nv) ? ld_stream(vp + vi * E) : zero_vec();
+        }
       }
     }
 #pragma unroll
@@ -85,6 +119,13 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
           for (int e = 0; e < E; ++e) {
             const float sv = __fadd_rn(v[i][e], rv[e]);
             v[i][e] = round_sum ? round_to<T>(sv) : sv;
+          }
+          if constexpr (DS) {
+            if (dj[b] >= 0) {
+              unpack<T>(dr[b][i], rv);
+#pragma unroll
+              for (int e = 0; e < E; ++e) v[i][e] = round_to<T>(__fadd_rn(v[i][e], rv[e]));
+            }
           }
         }
         ss = __fadd_rn(ss, sumsq_tree<E>(v[i]));
@@ -114,11 +155,11 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
 }
 
 // One CTA per row (rows longer than 256 vectors); VPT vectors per thread.
-template <typename T, typename W, int VPT>
+template <typename T, typename W, int VPT, bool DS = false>
 __global__ void __launch_bounds__(1024)
 rms_rows_block(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __restrict__ res,
                int64_t r_rs, const W* __restrict__ w, T* __restrict__ y, T* __restrict__ res_out,
-               int64_t rows, int64_t heads, int n, float eps, int add, int round_sum) {
+               int64_t rows, int64_t heads, int n, float eps, int add, int round_sum, DsArgs ds) {
   constexpr int E = Elem<T>::kPerVec;
   __shared__ float red[32];
   const int nv = n / E;
@@ -128,13 +169,23 @@ rms_rows_block(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __r
     const int64_t h = r - t * heads;
     const T* xp = x + t * x_ts + h * x_hs;
     const T* rp = add ? res + t * r_rs : nullptr;
-    uint4 xr[VPT], rr[VPT];
+    uint4 xr[VPT], rr[VPT], dr[DS ? VPT : 1];
+    int64_t dj = -1;
+    if constexpr (DS) dj = ds_row(ds, t);  // heads == 1
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = i * blockDim.x + threadIdx.x;
       const bool ok = vi < nv;
       xr[i] = ok ? ld_stream(xp + vi * E) : zero_vec();
       rr[i] = (ok && add) ? ld_stream(rp + vi * E) : zero_vec();
+    }
+    if constexpr (DS) {
+      const T* vp = static_cast<const T*>(ds.vis) + (dj >= 0 ? dj : 0) * ds.vis_rs;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int vi = i * blockDim.x + threadIdx.x;
+        dr[i] = (dj >= 0 && vi < nv) ? ld_stream(vp + vi * E) : zero_vec();
+      }
     }
     float v[VPT][E];
     float ss = 0.f;
@@ -148,6 +199,13 @@ rms_rows_block(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __r
         for (int e = 0; e < E; ++e) {
           const float s = __fadd_rn(v[i][e], rv[e]);
           v[i][e] = round_sum ? round_to<T>(s) : s;
+        }
+        if constexpr (DS) {
+          if (dj >= 0) {
+            unpack<T>(dr[i], rv);
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[i][e] = round_to<T>(__fadd_rn(v[i][e], rv[e]));
+          }
         }
       }
       ss = __fadd_rn(ss, sumsq_tree<E>(v[i]));
@@ -175,10 +233,10 @@ rms_rows_block(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __r
   }
 }
 
-template <typename T, typename W, int G, int VPT, int RB = 1>
+template <typename T, typename W, int G, int VPT, int RB = 1, bool DS = false>
 static void launch_warp(const void* x, int64_t x_ts, int64_t x_hs, const void* res, int64_t r_rs,
                         const void* w, void* y, void* res_out, int64_t rows, int64_t heads, int n,
-                        float eps, int add, int round_sum, cudaStream_t st) {
+                        float eps, int add, int round_sum, cudaStream_t st, const DsArgs& ds) {
   constexpr int kThreads = 256;
   constexpr int rows_per_block = (kThreads / 32) * (32 / G) * RB;
   int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
@@ -188,36 +246,37 @@ static void launch_warp(const void* x, int64_t x_ts, int64_t x_hs, const void* r
   const int64_t cap = G < 32 ? static_cast<int64_t>(sm_count()) * 32 : kMaxGrid;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  rms_rows_warp<T, W, G, VPT, RB><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+  rms_rows_warp<T, W, G, VPT, RB, DS><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
       static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
       static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
-      add, round_sum);
+      add, round_sum, ds);
 }
 
-template <typename T, typename W>
+template <typename T, typename W, bool DS>
 static int launch_rms(const void* x, int64_t x_ts, int64_t x_hs, const void* res, int64_t r_rs,
                       const void* w, void* y, void* res_out, int64_t rows, int64_t heads,
-                      int64_t n64, float eps, int add, int round_sum, cudaStream_t st) {
+                      int64_t n64, float eps, int add, int round_sum, cudaStream_t st,
+                      const DsArgs& ds) {
   constexpr int E = Elem<T>::kPerVec;
   const int n = static_cast<int>(n64);
   const int nv = n / E;
-  if (nv <= 32 && !add) {
+  if constexpr (!DS) if (nv <= 32 && !add) {
     // short rows (attention heads, q/k norm): G lanes x 2 vectors, lane g owns
     // vectors g and g + G - the rotate-half partners when a row is one head.
     // The fused attention prologue uses the same layout and summation order.
     const int half = (nv + 1) / 2;
-    if (half <= 1) launch_warp<T, W, 1, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (half <= 2) launch_warp<T, W, 2, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (half <= 4) launch_warp<T, W, 4, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else if (half <= 8) launch_warp<T, W, 8, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
-    else launch_warp<T, W, 16, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    if (half <= 1) launch_warp<T, W, 1, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st, ds);
+    else if (half <= 2) launch_warp<T, W, 2, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st, ds);
+    else if (half <= 4) launch_warp<T, W, 4, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st, ds);
+    else if (half <= 8) launch_warp<T, W, 8, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st, ds);
+    else launch_warp<T, W, 16, 2, 8>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st, ds);
     return launch_status("rms_norm");
   }
   if (nv <= 256) {
     const int vpt = (nv + 31) / 32;
     switch (vpt) {
 #define NIB_RMS_VPT(V) \
-      case V: launch_warp<T, W, 32, V>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st); break;
+      case V: launch_warp<T, W, 32, V, 1, DS>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st, ds); break;
       NIB_RMS_VPT(1) NIB_RMS_VPT(2) NIB_RMS_VPT(3) NIB_RMS_VPT(4)
       NIB_RMS_VPT(5) NIB_RMS_VPT(6) NIB_RMS_VPT(7) NIB_RMS_VPT(8)
 #undef NIB_RMS_VPT
@@ -231,22 +290,22 @@ static int launch_rms(const void* x, int64_t x_ts, int64_t x_hs, const void* res
   const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / threads);
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  rms_rows_block<T, W, 4><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+  rms_rows_block<T, W, 4, DS><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
       static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
       static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
-      add, round_sum);
+      add, round_sum, ds);
   return launch_status("rms_norm");
 }
 
-template <typename T>
+template <typename T, bool DS = false>
 static int dispatch_weight(int weight_dtype, int dtype, const void* x, int64_t x_ts, int64_t x_hs,
                            const void* res, int64_t r_rs, const void* w, void* y, void* res_out,
                            int64_t rows, int64_t heads, int64_t n, float eps, int add,
-                           int round_sum, cudaStream_t st) {
+                           int round_sum, cudaStream_t st, const DsArgs& ds = DsArgs{}) {
   if (weight_dtype == dtype)
-    return launch_rms<T, T>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    return launch_rms<T, T, DS>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st, ds);
   if (weight_dtype == NIB_F32)
-    return launch_rms<T, float>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st);
+    return launch_rms<T, float, DS>(x, x_ts, x_hs, res, r_rs, w, y, res_out, rows, heads, n, eps, add, round_sum, st, ds);
   set_error("rms_norm: weight dtype %d must equal the activation dtype %d or be float32", weight_dtype, dtype);
   return NIB_ERR_UNSUPPORTED;
 }
@@ -303,5 +362,45 @@ extern "C" int nib_add_rms_norm(int dtype, const void* x, int64_t x_row_stride, 
                return dispatch_weight<T>(weight_dtype, dtype, x, x_row_stride, 0, residual,
                                          residual_row_stride, weight, out, residual_out, rows, 1, n,
                                          eps, 1, round_sum ? 1 : 0, as_stream(stream)));
+  return NIB_OK;
+}
+
+extern "C" int nib_add_rms_norm_deepstack(int dtype, const void* x, int64_t x_row_stride,
+                                          const void* residual, int64_t residual_row_stride,
+                                          int64_t rows, int64_t n, int weight_dtype,
+                                          const void* weight, float eps, const void* vis,
+                                          int64_t vis_row_stride, int64_t vis_rows,
+                                          const int32_t* index, void* out, void* residual_out,
+                                          unsigned int* status, void* stream) {
+  NIB_REQUIRE(rows >= 0 && n >= 1 && vis_rows >= 0, "add_rms_norm_deepstack: bad sizes");
+  if (rows == 0) return NIB_OK;
+  NIB_REQUIRE(x && residual && weight && out && residual_out && index,
+              "add_rms_norm_deepstack: null pointer");
+  NIB_REQUIRE(vis || vis_rows == 0, "add_rms_norm_deepstack: null visual embedding");
+  int rc = check_vec_rows(dtype, x, x_row_stride, 0, n, "add_rms_norm_deepstack input");
+  if (rc) return rc;
+  rc = check_vec_rows(dtype, residual, residual_row_stride, 0, n, "add_rms_norm_deepstack residual");
+  if (rc) return rc;
+  rc = check_vec_rows(dtype, out, 0, 0, n, "add_rms_norm_deepstack output");
+  if (rc) return rc;
+  rc = check_vec_rows(dtype, residual_out, 0, 0, n, "add_rms_norm_deepstack residual output");
+  if (rc) return rc;
+  if (vis_rows > 0) {
+    rc = check_vec_rows(dtype, vis, vis_row_stride, 0, n, "add_rms_norm_deepstack visual embedding");
+    if (rc) return rc;
+  }
+  NIB_SUPPORT(aligned16(weight), "add_rms_norm_deepstack: weight is not 16-byte aligned");
+  NIB_SUPPORT(dtype != NIB_F32 || weight_dtype == NIB_F32,
+              "add_rms_norm_deepstack: float32 input needs float32 weight");
+  DsArgs ds;
+  ds.vis = vis;
+  ds.vis_rs = vis_row_stride;
+  ds.vis_rows = vis_rows;
+  ds.index = index;
+  ds.status = status;
+  NIB_DISPATCH(dtype, T,
+               return dispatch_weight<T, true>(weight_dtype, dtype, x, x_row_stride, 0, residual,
+                                               residual_row_stride, weight, out, residual_out, rows,
+                                               1, n, eps, 1, 1, as_stream(stream), ds));
   return NIB_OK;
 }

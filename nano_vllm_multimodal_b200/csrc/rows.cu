@@ -35,6 +35,27 @@ embedding_kernel(const int64_t* __restrict__ ids, int64_t n_ids, const char* __r
   }
 }
 
+// index[t] = -1 for every token, then index[rows[j]] = j (two launches on one stream)
+__global__ void __launch_bounds__(256)
+fill_index_kernel(int32_t* __restrict__ index, int64_t tokens) {
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < tokens;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    index[t] = -1;
+}
+__global__ void __launch_bounds__(256)
+scatter_index_kernel(const int64_t* __restrict__ rows, int64_t n_rows, int64_t tokens,
+                     int32_t* __restrict__ index, unsigned int* status) {
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < n_rows;
+       j += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = __ldg(rows + j);
+    if (r < 0 || r >= tokens) {
+      flag(status, NIB_DEV_BAD_INDEX);
+      continue;
+    }
+    index[r] = static_cast<int32_t>(j);
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256)
 deepstack_add_kernel(T* __restrict__ h, int64_t h_rs, int64_t tokens, int n,
@@ -140,6 +161,23 @@ extern "C" int nib_deepstack_add(int dtype, void* hidden, int64_t hidden_row_str
                    static_cast<T*>(hidden), hidden_row_stride, tokens, static_cast<int>(n), rows,
                    n_rows, static_cast<const T*>(vis), vis_row_stride, status));
   return launch_status("deepstack_add");
+}
+
+extern "C" int nib_deepstack_row_index(const int64_t* rows, int64_t n_rows, int64_t tokens,
+                                       int32_t* index, unsigned int* status, void* stream) {
+  NIB_REQUIRE(n_rows >= 0 && tokens >= 0 && n_rows <= INT32_MAX, "deepstack_row_index: bad sizes");
+  if (tokens == 0) return NIB_OK;
+  NIB_REQUIRE(index && (rows || n_rows == 0), "deepstack_row_index: null pointer");
+  const cudaStream_t st = as_stream(stream);
+  int64_t blocks = (tokens + 255) / 256;
+  if (blocks > kMaxGrid) blocks = kMaxGrid;
+  fill_index_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(index, tokens);
+  if (n_rows > 0) {
+    int64_t b2 = (n_rows + 255) / 256;
+    if (b2 > kMaxGrid) b2 = kMaxGrid;
+    scatter_index_kernel<<<static_cast<unsigned>(b2), 256, 0, st>>>(rows, n_rows, tokens, index, status);
+  }
+  return launch_status("deepstack_row_index");
 }
 
 extern "C" int nib_copy_rows(int dtype, const void* in, int64_t in_row_stride, int64_t rows,

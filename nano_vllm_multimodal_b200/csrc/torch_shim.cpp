@@ -410,6 +410,52 @@ void deepstack_add_(Tensor hidden, const Tensor& rows, const Tensor& vis, const 
         "nanoinfer_b200::deepstack_add_");
 }
 
+Tensor deepstack_row_index(const Tensor& rows, int64_t tokens, const optional<Tensor>& status) {
+  TORCH_CHECK(rows.scalar_type() == at::kLong && rows.dim() == 1, "deepstack_row_index: rows must be int64 [n]");
+  TORCH_CHECK(tokens >= 0, "deepstack_row_index: tokens must be >= 0");
+  c10::cuda::CUDAGuard guard(rows.device());
+  Tensor index = at::empty({tokens}, rows.options().dtype(at::kInt));
+  if (tokens == 0) return index;
+  Tensor rc = rows.contiguous();
+  check(nib_deepstack_row_index(rc.data_ptr<int64_t>(), rc.numel(), tokens, index.data_ptr<int32_t>(),
+                                status_ptr(status), stream_of(rows)),
+        "nanoinfer_b200::deepstack_row_index");
+  return index;
+}
+
+std::tuple<Tensor, Tensor> add_rms_norm_deepstack(const Tensor& x, const Tensor& residual,
+                                                  const Tensor& weight, double eps, const Tensor& vis,
+                                                  const Tensor& index, const optional<Tensor>& status) {
+  TORCH_CHECK(x.dim() == 2 && x.sizes() == residual.sizes(),
+              "add_rms_norm_deepstack: x and residual must be [tokens, hidden] of one shape");
+  TORCH_CHECK(x.scalar_type() == residual.scalar_type() && vis.scalar_type() == x.scalar_type(),
+              "add_rms_norm_deepstack: x, residual and the visual embedding must share a dtype");
+  TORCH_CHECK(x.stride(1) == 1 && residual.stride(1) == 1, "add_rms_norm_deepstack: last dim must be contiguous");
+  const int64_t n = x.size(1);
+  TORCH_CHECK(vis.dim() == 2 && vis.size(1) == n && (vis.size(0) == 0 || vis.stride(1) == 1),
+              "add_rms_norm_deepstack: visual embedding must be [rows, hidden]");
+  TORCH_CHECK(index.scalar_type() == at::kInt && index.dim() == 1 && index.size(0) == x.size(0),
+              "add_rms_norm_deepstack: index must be int32 [tokens]");
+  TORCH_CHECK(weight.numel() == n, "add_rms_norm_deepstack: weight size mismatch");
+  on_device(x, residual, "add_rms_norm_deepstack residual");
+  on_device(x, weight, "add_rms_norm_deepstack weight");
+  on_device(x, vis, "add_rms_norm_deepstack visual embedding");
+  on_device(x, index, "add_rms_norm_deepstack index");
+  c10::cuda::CUDAGuard guard(x.device());
+  Tensor y = at::empty(x.sizes(), x.options().memory_format(at::MemoryFormat::Contiguous));
+  Tensor r = at::empty(x.sizes(), x.options().memory_format(at::MemoryFormat::Contiguous));
+  if (x.numel() == 0) return {y, r};
+  Tensor w = weight.contiguous();
+  Tensor ic = index.contiguous();
+  check(nib_add_rms_norm_deepstack(code_of(x.scalar_type()), x.data_ptr(), x.stride(0), residual.data_ptr(),
+                                   residual.stride(0), x.size(0), n, code_of(w.scalar_type()), w.data_ptr(),
+                                   static_cast<float>(eps), vis.numel() ? vis.data_ptr() : nullptr,
+                                   vis.numel() ? vis.stride(0) : n, vis.size(0), ic.data_ptr<int32_t>(),
+                                   y.data_ptr(), r.data_ptr(), status_ptr(status), stream_of(x)),
+        "nanoinfer_b200::add_rms_norm_deepstack");
+  return {y, r};
+}
+
 Tensor deepstack_add(const Tensor& hidden, const Tensor& rows, const Tensor& vis,
                      const optional<Tensor>& status) {
   TORCH_CHECK(hidden.dim() == 2 && hidden.stride(1) == 1, "deepstack_add: hidden must be [tokens, hidden]");
@@ -576,6 +622,9 @@ TORCH_LIBRARY(nanoinfer_b200, m) {
   m.def("embedding(Tensor ids, Tensor weight, int vocab_start, int vocab_end, bool mask, "
         "Tensor(a!)? status) -> Tensor");
   m.def("deepstack_add(Tensor hidden, Tensor rows, Tensor vis, Tensor(a!)? status) -> Tensor");
+  m.def("deepstack_row_index(Tensor rows, int tokens, Tensor(a!)? status) -> Tensor");
+  m.def("add_rms_norm_deepstack(Tensor x, Tensor residual, Tensor weight, float eps, Tensor vis, "
+        "Tensor index, Tensor(a!)? status) -> (Tensor, Tensor)");
   m.def("deepstack_add_(Tensor(a!) hidden, Tensor rows, Tensor vis, Tensor(b!)? status) -> ()");
 }
 
@@ -590,4 +639,6 @@ TORCH_LIBRARY_IMPL(nanoinfer_b200, CUDA, m) {
   m.impl("embedding", TORCH_FN(nib_torch::embedding));
   m.impl("deepstack_add", TORCH_FN(nib_torch::deepstack_add));
   m.impl("deepstack_add_", TORCH_FN(nib_torch::deepstack_add_));
+  m.impl("deepstack_row_index", TORCH_FN(nib_torch::deepstack_row_index));
+  m.impl("add_rms_norm_deepstack", TORCH_FN(nib_torch::add_rms_norm_deepstack));
 }

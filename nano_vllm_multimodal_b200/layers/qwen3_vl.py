@@ -17,6 +17,12 @@ class Qwen3VLTextRMSNorm(nn.Module):
     Qwen3-VL decoder's separate ``hidden + residual`` (one dtype rounding,
     ``qwen3_vl.py:232-237``) into the same pass and returns
     ``(normed, hidden + residual)``.
+
+    ``forward(x, residual, deepstack=(visual_embedding, row_index))`` also folds
+    the DeepStack add that the reference applies to the previous layer's output
+    (``qwen3_vl.py:371-376``): tokens with ``row_index[t] >= 0`` add
+    ``visual_embedding[row_index[t]]`` to the rounded sum before the norm.
+    ``row_index`` comes from :func:`deepstack_row_index`.
     """
 
     def __init__(self, hidden_size: int, eps: float = 1e-6) -> None:
@@ -29,11 +35,25 @@ class Qwen3VLTextRMSNorm(nn.Module):
             raise TypeError("Qwen3VLTextRMSNorm: weight dtype must match the activations "
                             f"({self.weight.dtype} vs {x.dtype})")
 
-    def forward(self, hidden_states: torch.Tensor, residual: torch.Tensor | None = None):
+    def forward(self, hidden_states: torch.Tensor, residual: torch.Tensor | None = None,
+                deepstack: tuple[torch.Tensor, torch.Tensor] | None = None):
         self._check_dtype(hidden_states)
+        if deepstack is not None:
+            if residual is None:
+                raise ValueError("Qwen3VLTextRMSNorm: the DeepStack fold needs the residual")
+            visual_embedding, row_index = deepstack
+            return ops.add_rms_norm_deepstack(hidden_states, residual, self.weight, self.eps,
+                                              visual_embedding, row_index)
         if residual is None:
             return ops.rms_norm(hidden_states, self.weight, self.eps)
         return ops.add_rms_norm(hidden_states, residual, self.weight, self.eps, round_sum=True)
+
+
+def deepstack_row_index(visual_token_rows: torch.Tensor, num_tokens: int) -> torch.Tensor:
+    """Token -> visual-row map (int32 ``[num_tokens]``, ``-1`` for text tokens) for
+    ``Qwen3VLTextRMSNorm.forward(..., deepstack=...)``. The rows are the same for
+    the three DeepStack layers, so one map serves all of them."""
+    return ops.deepstack_row_index(visual_token_rows, num_tokens)
 
 
 def add_deepstack_rows(hidden_states: torch.Tensor, visual_token_rows: torch.Tensor,

@@ -211,3 +211,24 @@ def deepstack_add_(hidden, rows, vis) -> torch.Tensor:
     _ops().deepstack_add_(hidden, rows, vis, st)
     _check_status(st, "deepstack_add_")
     return hidden
+
+
+def deepstack_row_index(rows, tokens: int) -> torch.Tensor:
+    """int32 ``[tokens]``: ``j`` at ``rows[j]``, ``-1`` elsewhere (the map the
+    folded add + norm + DeepStack kernel reads; build once per forward)."""
+    st = _status_for(rows)
+    out = _ops().deepstack_row_index(rows, int(tokens), st)
+    _check_status(st, "deepstack_row_index")
+    return out
+
+
+def add_rms_norm_deepstack(x, residual, weight, eps, vis, row_index):
+    """Qwen3-VL layer boundary in one pass -> ``(normed, new_residual)``:
+    ``s = dtype(x + residual)``; tokens with ``row_index[t] >= 0`` add
+    ``vis[row_index[t]]`` (one more rounding); ``normed = Qwen3VLTextRMSNorm(s)``.
+    Equals ``add_rms_norm(..., round_sum=True)`` after ``deepstack_add_`` on the sum
+    (``nanovllm/models/qwen3_vl.py:238,332-344,371-376`` then ``:232-235``)."""
+    st = _status_for(x)
+    out = _ops().add_rms_norm_deepstack(x, residual, weight, float(eps), vis, row_index, st)
+    _check_status(st, "add_rms_norm_deepstack")
+    return out

@@ -22,6 +22,7 @@ __all__ = [
     "rms_norm",
     "text_rms_norm",
     "add_text_rms_norm",
+    "add_text_rms_norm_deepstack",
     "silu_and_mul",
     "silu_and_mul_fp32",
     "rope_cos_sin_cache",
@@ -418,6 +419,28 @@ def add_deepstack_rows(hidden_states, visual_token_rows, visual_embedding):
 
 
 # --------------------------------------------------------------------------- compositions
+
+
+def add_text_rms_norm_deepstack(x, residual, weight, eps, visual_token_rows, visual_embedding,
+                                order="torch"):
+    """Qwen3-VL layer boundary with a DeepStack layer in between.
+
+    The layer's output add ``mlp_residual + mlp(h)`` (``nanovllm/models/qwen3_vl.py:238``,
+    one dtype rounding), then ``_add_deepstack_rows`` on that output
+    (``:332-344``, called at ``:371-376``), then the next layer's
+    ``input_layernorm`` (``:234``, ``Qwen3VLTextRMSNorm`` ``:74-79``), whose
+    ``attention_residual`` is the DeepStack-updated sum. Returns
+    ``(normed, updated_sum)``.
+    """
+    s = _round(x.float() + residual.float(), x.dtype)
+    s = add_deepstack_rows(s, visual_token_rows, visual_embedding)
+    if order == "torch":
+        return text_rms_norm(s, weight, eps), s
+    sf = s.float()
+    n = _round(sf * _inv_rms(sf, eps, order, x.dtype, add=True), x.dtype)
+    out_dtype = torch.promote_types(weight.dtype, x.dtype)
+    return _round(weight.float() * n.float(), out_dtype).contiguous(), s
+
 
 
 def qk_norm_rope_store(
