@@ -473,6 +473,64 @@ def _time_op(fn, reps=20, warmup=3, flush=None):
     return total / reps
 
 
+def visual_merge_component(out, record, flush, seeds, rows, c3):
+    """Packed-prefill visual merge at C3: 16 images x 1,024 rows, 3 DeepStack layers.
+    Kernel alone (plan packed once), the whole API call (host packing included) and
+    the reference's own torch path (model_runner.py:237-285, restated inline)."""
+    from types import SimpleNamespace
+
+    from nano_vllm_multimodal_b200 import ops
+    from nano_vllm_multimodal_b200.layers.visual_merge import build_planned_visual_embeddings
+    from nano_vllm_multimodal_b200 import workloads as W
+
+    T, H, L, per = c3.tokens, c3.hidden, 3, 1024
+    tok = W._normal(seeds, (T, H))
+    feats = {}
+    for i in range(rows.numel() // per):
+        f = W._normal(seeds, (L + 1, per, H))
+        feats[f"vision:{i}"] = SimpleNamespace(final_embedding=f[0], deepstack_embeddings=tuple(f[1:]))
+    reps = tuple(SimpleNamespace(output_row=r, feature_key=f"vision:{i // per}", feature_row=i % per)
+                 for i, r in enumerate(rows.tolist()))
+    plan = SimpleNamespace(replacements=reps)
+    R = len(reps)
+    # kernel alone: the device plan and table that the API call packs
+    table = torch.zeros(len(feats), 20, dtype=torch.int64)
+    for k, b in enumerate(feats.values()):
+        table[k, 0], table[k, 1], table[k, 2], table[k, 3] = b.final_embedding.data_ptr(), H, per, 2
+        for l, d in enumerate(b.deepstack_embeddings):
+            table[k, 4 + l], table[k, 12 + l] = d.data_ptr(), H
+    plan_dev = torch.tensor([r.output_row for r in reps] + [i // per for i in range(R)]
+                            + [i % per for i in range(R)], dtype=torch.int64, device=tok.device)
+    table_dev = table.to(tok.device)
+    ms = _time_op(flush=flush, fn=lambda: ops.visual_merge(tok, table_dev, L, plan_dev, R))
+    record("visual_merge", ms, 4 * H * (T + R * L),
+           "C3: [32768,2048] tokens, 16 x 1024 image rows, 3 DeepStack layers; kernel alone")
+    ms_api = _time_op(flush=flush, fn=lambda: build_planned_visual_embeddings(tok, plan, feats))
+
+    def reference_path():
+        merged = tok.clone()
+        ds = tuple(torch.empty((R, H), device=tok.device, dtype=tok.dtype) for _ in range(L))
+        groups = {}
+        for idx, rp in enumerate(reps):
+            groups.setdefault(rp.feature_key, []).append((idx, rp))
+        for key, grouped in groups.items():
+            b = feats[key]
+            out_rows = torch.tensor([rp.output_row for _, rp in grouped], dtype=torch.int64, device=tok.device)
+            frows = torch.tensor([rp.feature_row for _, rp in grouped], dtype=torch.int64, device=tok.device)
+            merged.index_copy_(0, out_rows, b.final_embedding.index_select(0, frows).to(tok.dtype))
+            vrows = torch.tensor([i for i, _ in grouped], dtype=torch.int64, device=tok.device)
+            for l, emb in enumerate(b.deepstack_embeddings):
+                lrows = torch.tensor([rp.feature_row for _, rp in grouped], dtype=torch.int64, device=tok.device)
+                ds[l].index_copy_(0, vrows, emb.index_select(0, lrows).to(tok.dtype))
+        return merged, ds
+
+    ms_ref = _time_op(flush=flush, fn=reference_path)
+    out["visual_merge"]["api_ms"] = round(ms_api, 4)
+    out["visual_merge"]["reference_torch_ms"] = round(ms_ref, 4)
+    out["visual_merge"]["note"] = ("api_ms: build_planned_visual_embeddings incl. host plan packing; "
+                                   "reference_torch_ms: the reference's per-key index_select/index_copy_ path")
+
+
 def component_bench(inp, device, hbm_peak):
     """The path's kernels that the fused layer does not exercise on their own,
     each at a full config size, timed with CUDA events (working sets > L2)."""
@@ -531,6 +589,7 @@ def component_bench(inp, device, hbm_peak):
     out["add_norm_deepstack"]["unfused_ms"] = round(ms_unfused, 4)
     out["add_norm_deepstack"]["unfused"] = "torch add + deepstack_add_ + rms_norm"
     del hs, vis, res
+    visual_merge_component(out, record, flush, seeds, rows, c3)
     # generic M-RoPE apply on materialised cos/sin (apply_multimodal_rotary_emb)
     pos = inp["positions"][:, :32768]
     qq = q[:32768]

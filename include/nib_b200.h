@@ -98,6 +98,44 @@ NIB_API int nib_add_rms_norm_deepstack(int dtype, const void* x, int64_t x_row_s
                                const int32_t* index, void* out, void* residual_out,
                                unsigned int* status, void* stream);
 
+/* ------------------------------------------------------------------ visual merge */
+
+#define NIB_VISUAL_MAX_LAYERS 8
+
+/* One vision-feature source (one feature key of the reference's plan): its
+ * final embedding rows and, per DeepStack layer, the rows of that layer (same
+ * row count). Row strides in elements; dtype is a nib_dtype. Lives in device
+ * memory (an array of these is read by the kernel). 160 bytes. */
+typedef struct nib_visual_source {
+  const void* final_rows;
+  int64_t final_row_stride;
+  int64_t final_count;
+  int32_t dtype;
+  int32_t reserved;
+  const void* deepstack[NIB_VISUAL_MAX_LAYERS];
+  int64_t deepstack_row_stride[NIB_VISUAL_MAX_LAYERS];
+} nib_visual_source;
+
+/* Packed-prefill visual merge. For replacement i < num_replacements (device
+ * arrays): merged[output_rows[i]] = sources[source_index[i]].final_rows[feature_rows[i]],
+ * and for every layer l < num_layers:
+ * deepstack_out[l, i] = sources[source_index[i]].deepstack[l][feature_rows[i]].
+ * Every other merged row is the token embedding row. merged is contiguous
+ * [tokens, hidden] of `dtype`; deepstack_out contiguous [num_layers,
+ * num_replacements, hidden]. Source rows of another dtype are converted (fp32
+ * round trip, round to nearest). row_map: device scratch of `tokens` int32.
+ * Out-of-range output rows, sources or feature rows set NIB_DEV_BAD_INDEX in
+ * *status (when given); their rows are skipped (output rows) or zero-filled.
+ * Three launches, no allocation, no synchronisation.
+ * Replaces: build_planned_visual_embeddings / merge_planned_visual_embeddings
+ * nanovllm/engine/model_runner.py:158-286 (per-key index_select/index_copy_) */
+NIB_API int nib_visual_merge(int dtype, const void* token_embeddings, int64_t token_row_stride,
+                     int64_t tokens, int64_t hidden, const nib_visual_source* sources,
+                     int64_t num_sources, int num_layers, const int64_t* output_rows,
+                     const int64_t* source_index, const int64_t* feature_rows,
+                     int64_t num_replacements, int32_t* row_map, void* merged,
+                     void* deepstack_out, unsigned int* status, void* stream);
+
 /* ------------------------------------------------------------------ activation */
 
 /* y[t, :] = silu(x[t, :I]) * x[t, I:2I], computed in fp32, rounded once.

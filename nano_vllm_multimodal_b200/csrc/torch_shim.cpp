@@ -456,6 +456,35 @@ std::tuple<Tensor, Tensor> add_rms_norm_deepstack(const Tensor& x, const Tensor&
   return {y, r};
 }
 
+// plan: int64 [3 * R] on the device (output rows | source index | feature rows);
+// table: int64 [K, sizeof(nib_visual_source) / 8] on the device
+std::tuple<Tensor, Tensor> visual_merge(const Tensor& tokens, const Tensor& table, int64_t num_layers,
+                                        const Tensor& plan, int64_t num_replacements,
+                                        const optional<Tensor>& status) {
+  TORCH_CHECK(tokens.dim() == 2 && (tokens.size(0) == 0 || tokens.stride(1) == 1),
+              "visual_merge: token embeddings must be [tokens, hidden] with a contiguous last dim");
+  TORCH_CHECK(table.scalar_type() == at::kLong && table.dim() == 2 &&
+                  table.size(1) * 8 == static_cast<int64_t>(sizeof(nib_visual_source)) && table.is_contiguous(),
+              "visual_merge: bad source table");
+  TORCH_CHECK(plan.scalar_type() == at::kLong && plan.is_contiguous() && plan.numel() >= 3 * num_replacements,
+              "visual_merge: bad plan");
+  TORCH_CHECK(num_layers >= 0 && num_layers <= NIB_VISUAL_MAX_LAYERS, "visual_merge: too many DeepStack layers");
+  on_device(tokens, table, "visual_merge source table");
+  on_device(tokens, plan, "visual_merge plan");
+  c10::cuda::CUDAGuard guard(tokens.device());
+  const int64_t T = tokens.size(0), H = tokens.size(1), R = num_replacements;
+  Tensor merged = at::empty({T, H}, tokens.options());
+  Tensor ds = at::empty({num_layers, R, H}, tokens.options());
+  Tensor row_map = at::empty({T}, tokens.options().dtype(at::kInt));
+  const int64_t* pp = plan.data_ptr<int64_t>();
+  check(nib_visual_merge(code_of(tokens.scalar_type()), tokens.data_ptr(), T ? tokens.stride(0) : H, T, H,
+                         reinterpret_cast<const nib_visual_source*>(table.data_ptr<int64_t>()), table.size(0),
+                         static_cast<int>(num_layers), pp, pp + R, pp + 2 * R, R, row_map.data_ptr<int32_t>(),
+                         merged.data_ptr(), ds.data_ptr(), status_ptr(status), stream_of(tokens)),
+        "nanoinfer_b200::visual_merge");
+  return {merged, ds};
+}
+
 Tensor deepstack_add(const Tensor& hidden, const Tensor& rows, const Tensor& vis,
                      const optional<Tensor>& status) {
   TORCH_CHECK(hidden.dim() == 2 && hidden.stride(1) == 1, "deepstack_add: hidden must be [tokens, hidden]");
@@ -623,6 +652,8 @@ TORCH_LIBRARY(nanoinfer_b200, m) {
         "Tensor(a!)? status) -> Tensor");
   m.def("deepstack_add(Tensor hidden, Tensor rows, Tensor vis, Tensor(a!)? status) -> Tensor");
   m.def("deepstack_row_index(Tensor rows, int tokens, Tensor(a!)? status) -> Tensor");
+  m.def("visual_merge(Tensor tokens, Tensor table, int num_layers, Tensor plan, int num_replacements, "
+        "Tensor(a!)? status) -> (Tensor, Tensor)");
   m.def("add_rms_norm_deepstack(Tensor x, Tensor residual, Tensor weight, float eps, Tensor vis, "
         "Tensor index, Tensor(a!)? status) -> (Tensor, Tensor)");
   m.def("deepstack_add_(Tensor(a!) hidden, Tensor rows, Tensor vis, Tensor(b!)? status) -> ()");
@@ -640,5 +671,6 @@ TORCH_LIBRARY_IMPL(nanoinfer_b200, CUDA, m) {
   m.impl("deepstack_add", TORCH_FN(nib_torch::deepstack_add));
   m.impl("deepstack_add_", TORCH_FN(nib_torch::deepstack_add_));
   m.impl("deepstack_row_index", TORCH_FN(nib_torch::deepstack_row_index));
+  m.impl("visual_merge", TORCH_FN(nib_torch::visual_merge));
   m.impl("add_rms_norm_deepstack", TORCH_FN(nib_torch::add_rms_norm_deepstack));
 }

@@ -12,6 +12,9 @@ hot-path names that the decoder models import at module load:
 * ``nanovllm.layers.attention.store_kvcache``
 * ``nanovllm.models.qwen3_vl.Qwen3VLTextRMSNorm`` and
   ``Qwen3VLLanguageModel._add_deepstack_rows``
+* ``nanovllm.engine.model_runner.{build_planned_visual_embeddings,
+  merge_planned_visual_embeddings}`` (the packed-prefill visual merge, one
+  kernel; results are the reference's own ``PlannedVisualEmbeddings``)
 * ``nanovllm.layers.paged_kv.loader.load_paged_kv_extension`` - so the
   reference's own ``CUDAPagedKVBackend`` gets ``torch.ops.nanovllm_paged_kv``
   and ``PagedKVCache`` from this package's extension instead of JIT-building
@@ -33,10 +36,19 @@ def _targets():
     from nano_vllm_multimodal_b200._lib import load_ops
     from nano_vllm_multimodal_b200.layers import activation, attention, embed_head, layernorm
     from nano_vllm_multimodal_b200.layers import multimodal_rotary_embedding as mrope
-    from nano_vllm_multimodal_b200.layers import qwen3_vl, rotary_embedding
+    from nano_vllm_multimodal_b200.layers import qwen3_vl, rotary_embedding, visual_merge
 
     def load_paged_kv_extension(*, verbose: bool = False) -> None:
         load_ops()
+
+    def build_planned_visual_embeddings(token_embeddings, plan, features):
+        runner = sys.modules.get("nanovllm.engine.model_runner")
+        result_type = getattr(runner, "PlannedVisualEmbeddings", visual_merge.PlannedVisualEmbeddings)
+        return visual_merge.build_planned_visual_embeddings(token_embeddings, plan, features,
+                                                            result_type=result_type)
+
+    def merge_planned_visual_embeddings(token_embeddings, plan, features):
+        return build_planned_visual_embeddings(token_embeddings, plan, features).final_embedding
 
     return {
         "nanovllm.layers.layernorm": {"RMSNorm": layernorm.RMSNorm},
@@ -52,6 +64,9 @@ def _targets():
         "nanovllm.layers.paged_kv.loader": {"load_paged_kv_extension": load_paged_kv_extension},
         "nanovllm.layers.paged_kv.cuda_backend": {"load_paged_kv_extension": load_paged_kv_extension},
         "nanovllm.models.qwen3_vl": {"Qwen3VLTextRMSNorm": qwen3_vl.Qwen3VLTextRMSNorm},
+        "nanovllm.engine.model_runner": {
+            "build_planned_visual_embeddings": build_planned_visual_embeddings,
+            "merge_planned_visual_embeddings": merge_planned_visual_embeddings},
     }
 
 

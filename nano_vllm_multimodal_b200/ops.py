@@ -213,6 +213,17 @@ def deepstack_add_(hidden, rows, vis) -> torch.Tensor:
     return hidden
 
 
+def visual_merge(token_embeddings, table, num_layers: int, plan, num_replacements: int):
+    """Packed-prefill visual merge (``nib_visual_merge``) -> ``(merged, deepstack)``,
+    ``deepstack`` being ``[num_layers, num_replacements, hidden]``. ``table`` and
+    ``plan`` are the device int64 buffers that
+    ``layers.visual_merge.build_planned_visual_embeddings`` packs."""
+    st = _status_for(token_embeddings)
+    out = _ops().visual_merge(token_embeddings, table, int(num_layers), plan, int(num_replacements), st)
+    _check_status(st, "visual_merge")
+    return out
+
+
 def deepstack_row_index(rows, tokens: int) -> torch.Tensor:
     """int32 ``[tokens]``: ``j`` at ``rows[j]``, ``-1`` elsewhere (the map the
     folded add + norm + DeepStack kernel reads; build once per forward)."""

@@ -23,6 +23,7 @@ __all__ = [
     "text_rms_norm",
     "add_text_rms_norm",
     "add_text_rms_norm_deepstack",
+    "planned_visual_embeddings",
     "silu_and_mul",
     "silu_and_mul_fp32",
     "rope_cos_sin_cache",
@@ -416,6 +417,33 @@ def add_deepstack_rows(hidden_states, visual_token_rows, visual_embedding):
     out = hidden_states.clone()
     out.index_copy_(0, rows, updated)
     return out
+
+
+# --------------------------------------------------------------------------- visual merge
+
+
+def planned_visual_embeddings(token_embeddings, replacements, features):
+    """``build_planned_visual_embeddings``: ``nanovllm/engine/model_runner.py:170-286``.
+
+    ``replacements``: ``(output_row, feature_key, feature_row)`` in plan order;
+    ``features``: key -> ``(final, (deepstack_0, ...))``. The merged tensor is a
+    copy of the token embeddings with row ``output_row`` taken from
+    ``final[feature_row]``; DeepStack payload ``l`` holds
+    ``deepstack_l[feature_row]`` at the replacement's plan index. Feature rows
+    are converted to the token dtype (``.to(dtype)``). Returns
+    ``(merged, payloads, visual_rows)``.
+    """
+    merged = token_embeddings.clone()
+    layers = len(next(iter(features.values()))[1]) if replacements else 0
+    payloads = tuple(torch.empty(len(replacements), merged.shape[1], dtype=merged.dtype)
+                     for _ in range(layers))
+    for i, (out_row, key, feat_row) in enumerate(replacements):
+        final, deepstack = features[key]
+        merged[out_row] = final[feat_row].to(merged.dtype)
+        for l in range(layers):
+            payloads[l][i] = deepstack[l][feat_row].to(merged.dtype)
+    rows = torch.tensor([r[0] for r in replacements], dtype=torch.int64)
+    return merged, payloads, rows
 
 
 # --------------------------------------------------------------------------- compositions

@@ -49,6 +49,8 @@ SOURCES = [
     "nanovllm/models/qwen3_vl.py",
     "nanovllm/models/qwen3.py",
     "nanovllm/models/qwen25_vl.py",
+    "nanovllm/engine/model_runner.py",
+    "nanovllm/multimodal/runtime.py",
 ]
 
 
@@ -59,7 +61,10 @@ def _ref():
         MultimodalRotaryEmbedding, apply_multimodal_rotary_emb)
     from nanovllm.layers.paged_kv.pytorch_backend import PyTorchPagedKVBackend
     from nanovllm.layers.rotary_embedding import RotaryEmbedding
+    from nanovllm.engine.model_runner import (
+        VisualReplacement, VisualReplacementPlan, build_planned_visual_embeddings)
     from nanovllm.models.qwen3_vl import Qwen3VLLanguageModel, Qwen3VLTextRMSNorm
+    from nanovllm.multimodal.runtime import VisionFeatureBundle
     with patch("torch.distributed.get_rank", return_value=0), \
             patch("torch.distributed.get_world_size", return_value=1):
         from nanovllm.layers.embed_head import VocabParallelEmbedding
@@ -67,7 +72,9 @@ def _ref():
                 MRoPE=MultimodalRotaryEmbedding, apply_mrope=apply_multimodal_rotary_emb,
                 Store=PyTorchPagedKVBackend, TextNorm=Qwen3VLTextRMSNorm,
                 add_deepstack=Qwen3VLLanguageModel._add_deepstack_rows,
-                Embedding=VocabParallelEmbedding)
+                Embedding=VocabParallelEmbedding, VisualReplacement=VisualReplacement,
+                VisualReplacementPlan=VisualReplacementPlan, Bundle=VisionFeatureBundle,
+                build_visual=build_planned_visual_embeddings)
 
 
 def _rms(R, hidden, weight, eps=1e-6):
@@ -209,6 +216,29 @@ def build():
     vis = torch.randn(rows.numel(), 256, generator=g).to(torch.bfloat16)
     cases["deepstack_c3"] = dict(inputs=dict(hidden=hs, rows=rows, vis=vis),
                                  outputs=dict(y=R["add_deepstack"](hs, rows, vis)), meta={})
+
+    # ---- (f) visual-embedding merge of a packed prefill: two feature keys interleaved in
+    # the plan, one of them float32 (converted to the bf16 token dtype), 3 DeepStack layers,
+    # feature rows offset as after a chunked prefill
+    g = torch.Generator().manual_seed(3200)
+    tok = torch.randn(40, 64, generator=g).to(torch.bfloat16)
+    fa = torch.randn(4, 12, 64, generator=g).to(torch.bfloat16)   # final + 3 layers
+    fb = torch.randn(4, 10, 64, generator=g)                      # float32
+    keys = ("vision:a", "vision:b")
+    plan_rows = ([(3 + i, 0, 2 + i) for i in range(6)] + [(10 + i, 1, i) for i in range(4)]
+                 + [(20 + i, 0, 8 + i) for i in range(4)])
+    plan = R["VisualReplacementPlan"](
+        replacements=tuple(R["VisualReplacement"](output_row=o, feature_key=keys[k], feature_row=f)
+                           for o, k, f in plan_rows),
+        required_feature_keys=keys, prefix_skipped_features=0)
+    bundles = {keys[0]: R["Bundle"](fa[0], tuple(fa[1:])), keys[1]: R["Bundle"](fb[0], tuple(fb[1:]))}
+    vm = R["build_visual"](tok, plan, bundles)
+    cases["visual_merge_c3"] = dict(
+        inputs=dict(tokens=tok, feature_a=fa, feature_b=fb,
+                    plan=torch.tensor(plan_rows, dtype=torch.int64)),
+        outputs=dict(final_embedding=vm.final_embedding, deepstack=torch.stack(vm.deepstack_embeddings),
+                     visual_rows=vm.visual_rows),
+        meta=dict(keys=keys))
 
     # ---- a8: fused attention prologues, composed from the reference modules
     def fused(dd, shape, norm_mod, rope_fn, slots_seed, skip):

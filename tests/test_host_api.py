@@ -163,3 +163,45 @@ def test_workload_shapes_and_determinism():
     assert torch.equal(c4["positions"][0, 8192:], c4["positions"][1, 8192:])
     tables = W.make_gather_inputs(5, sequences=3, seq_len=16384, num_blocks=1024)
     assert tables.shape == (3, 64) and all(t.unique().numel() == 64 for t in tables)
+
+
+# ------------------------------------------------ visual merge: host-side validation (no GPU)
+
+
+def _vm_plan(rows):
+    from types import SimpleNamespace
+    return SimpleNamespace(replacements=tuple(SimpleNamespace(output_row=o, feature_key=k, feature_row=f)
+                                              for o, k, f in rows))
+
+
+def test_visual_merge_validation_messages_match_reference():
+    """model_runner.py:175-235: the same exception types and messages, in the same order."""
+    from types import SimpleNamespace
+
+    from nano_vllm_multimodal_b200.layers.visual_merge import build_planned_visual_embeddings as build
+
+    tok = torch.zeros(5, 4)
+    with pytest.raises(ValueError, match=r"token embeddings must have shape \[tokens, hidden_size\]"):
+        build(torch.zeros(5), _vm_plan([(0, "a", 0)]), {})
+    # no replacements: the input object itself, no payloads, empty rows
+    out = build(tok, _vm_plan([]), {})
+    assert out.final_embedding is tok and out.deepstack_embeddings == () and out.visual_rows.numel() == 0
+    with pytest.raises(KeyError, match="missing visual feature: a"):
+        build(tok, _vm_plan([(0, "a", 0)]), {})
+    with pytest.raises(TypeError, match="visual feature must be a bundle: a"):
+        build(tok, _vm_plan([(0, "a", 0)]), {"a": [1, 2]})
+    with pytest.raises(ValueError, match="final vision embedding must be rank-2"):
+        build(tok, _vm_plan([(0, "a", 0)]), {"a": torch.zeros(4)})
+    with pytest.raises(ValueError, match="hidden size mismatch"):
+        build(tok, _vm_plan([(0, "a", 0)]), {"a": torch.zeros(2, 3)})
+    bundle1 = SimpleNamespace(final_embedding=torch.zeros(2, 4), deepstack_embeddings=(torch.zeros(2, 4),))
+    with pytest.raises(ValueError, match="deepstack layer count"):
+        build(tok, _vm_plan([(0, "a", 0), (1, "b", 0)]), {"a": bundle1, "b": torch.zeros(2, 4)})
+    with pytest.raises(IndexError, match="visual output row is out of range: 5"):
+        build(tok, _vm_plan([(5, "a", 0)]), {"a": torch.zeros(2, 4)})
+    with pytest.raises(IndexError, match="visual feature row is out of range: key=a, row=2"):
+        build(tok, _vm_plan([(0, "a", 2)]), {"a": torch.zeros(2, 4)})
+    too_deep = SimpleNamespace(final_embedding=torch.zeros(2, 4),
+                               deepstack_embeddings=tuple(torch.zeros(2, 4) for _ in range(9)))
+    with pytest.raises(NotImplementedError, match="at most 8 DeepStack layers"):
+        build(tok, _vm_plan([(0, "a", 0)]), {"a": too_deep})

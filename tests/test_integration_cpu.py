@@ -26,6 +26,17 @@ def fake_nanovllm(tmp_path, monkeypatch):
         "nanovllm/layers/paged_kv/__init__.py": "",
         "nanovllm/layers/paged_kv/loader.py": "def load_paged_kv_extension(*, verbose=False): raise RuntimeError('jit')\n",
         "nanovllm/layers/paged_kv/cuda_backend.py": "from nanovllm.layers.paged_kv.loader import load_paged_kv_extension\n",
+        "nanovllm/engine/__init__.py": "",
+        "nanovllm/engine/model_runner.py": textwrap.dedent("""
+            from dataclasses import dataclass
+            @dataclass(frozen=True)
+            class PlannedVisualEmbeddings:
+                final_embedding: object
+                deepstack_embeddings: tuple
+                visual_rows: object
+            def build_planned_visual_embeddings(t, p, f): raise RuntimeError('reference')
+            def merge_planned_visual_embeddings(t, p, f): raise RuntimeError('reference')
+        """),
         "nanovllm/models/__init__.py": "",
         "nanovllm/models/qwen3.py": textwrap.dedent("""
             from nanovllm.layers.layernorm import RMSNorm
@@ -69,3 +80,12 @@ def test_install_rebinds_hot_path_names(fake_nanovllm):
     assert q3vl.Qwen3VLLanguageModel._add_deepstack_rows is qwen3_vl.add_deepstack_rows
     assert "nanovllm.layers.paged_kv.loader.load_paged_kv_extension" in done
     assert cb.load_paged_kv_extension.__module__ == "nano_vllm_multimodal_b200.integration"
+    # the visual merge: rebound, and an empty plan returns the reference's result type
+    import nanovllm.engine.model_runner as mr
+    import torch
+    from types import SimpleNamespace
+    assert "nanovllm.engine.model_runner.build_planned_visual_embeddings" in done
+    tok = torch.zeros(3, 4)
+    res = mr.build_planned_visual_embeddings(tok, SimpleNamespace(replacements=()), {})
+    assert type(res) is mr.PlannedVisualEmbeddings and res.final_embedding is tok
+    assert mr.merge_planned_visual_embeddings(tok, SimpleNamespace(replacements=()), {}) is tok

@@ -104,6 +104,26 @@ def test_deepstack(golden):
     _eq(O.add_deepstack_rows(i["hidden"], i["rows"], i["vis"]), c["outputs"]["y"])
 
 
+def _visual_case(golden):
+    c = golden["visual_merge_c3"]
+    i = c["inputs"]
+    keys = c["meta"]["keys"]
+    feats = {keys[0]: (i["feature_a"][0], tuple(i["feature_a"][1:])),
+             keys[1]: (i["feature_b"][0], tuple(i["feature_b"][1:]))}
+    reps = [(int(o), keys[int(k)], int(f)) for o, k, f in i["plan"].tolist()]
+    return c, reps, feats
+
+
+def test_visual_merge(golden):
+    """build_planned_visual_embeddings golden (reference run): merged rows with a float32
+    source converted to bf16, three DeepStack payloads in plan order, visual rows."""
+    c, reps, feats = _visual_case(golden)
+    merged, payloads, rows = O.planned_visual_embeddings(c["inputs"]["tokens"], reps, feats)
+    assert torch.equal(merged.view(torch.int16), c["outputs"]["final_embedding"].view(torch.int16))
+    assert torch.equal(torch.stack(payloads).view(torch.int16), c["outputs"]["deepstack"].view(torch.int16))
+    assert torch.equal(rows, c["outputs"]["visual_rows"])
+
+
 @pytest.mark.parametrize("name", ["fused_qwen3_c1", "fused_qwen3vl_c3", "fused_qwen25vl_c4"])
 def test_fused_prologue(golden, name):
     c = golden[name]
