@@ -18,8 +18,10 @@ and one kernel launch writes every output row once (``nib_visual_merge``).
 
 from __future__ import annotations
 
+import operator
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from nano_vllm_multimodal_b200 import ops
@@ -74,17 +76,28 @@ def build_planned_visual_embeddings(token_embeddings: torch.Tensor, plan, featur
         return result_type(final_embedding=token_embeddings, deepstack_embeddings=(),
                            visual_rows=torch.empty(0, dtype=torch.int64, device=device))
     token_count, hidden_size = token_embeddings.shape
-    key_index: dict[str, int] = {}
+    reps = plan.replacements
+    n = len(reps)
+    # the plan's fields, extracted without a per-replacement Python loop body
+    out_rows = np.fromiter(map(operator.attrgetter("output_row"), reps), dtype=np.int64, count=n)
+    feat_rows = np.fromiter(map(operator.attrgetter("feature_row"), reps), dtype=np.int64, count=n)
+    keys = list(map(operator.attrgetter("feature_key"), reps))
+    key_index = {k: j for j, k in enumerate(dict.fromkeys(keys))}
+    source_index = np.fromiter(map(key_index.__getitem__, keys), dtype=np.int64, count=n)
+    _, first_seen = np.unique(source_index, return_index=True)  # first plan index of each key
+
+    # Validation with the reference's messages, raising the error its sequential
+    # loop (model_runner.py:190-235) meets first: the checks of a key run at that
+    # key's first replacement, before that replacement's row checks.
     sources: list[tuple[torch.Tensor, tuple[torch.Tensor, ...]]] = []
     layer_count = None
-    output_rows, source_index, feature_rows = [], [], []
-    for replacement in plan.replacements:
-        k = key_index.get(replacement.feature_key)
-        if k is None:
-            feature = features.get(replacement.feature_key)
+    key_error, key_error_at = None, n
+    for key, j in key_index.items():
+        try:
+            feature = features.get(key)
             if feature is None:
-                raise KeyError(f"missing visual feature: {replacement.feature_key}")
-            final, deepstack = _feature_parts(replacement.feature_key, feature)
+                raise KeyError(f"missing visual feature: {key}")
+            final, deepstack = _feature_parts(key, feature)
             if final.shape[1] != hidden_size:
                 raise ValueError("visual feature hidden size mismatch: "
                                  f"feature={tuple(final.shape)}, hidden_size={hidden_size}")
@@ -92,23 +105,29 @@ def build_planned_visual_embeddings(token_embeddings: torch.Tensor, plan, featur
                 layer_count = len(deepstack)
             elif layer_count != len(deepstack):
                 raise ValueError("visual features must have the same deepstack layer count")
-            k = len(sources)
-            key_index[replacement.feature_key] = k
-            sources.append((final, deepstack))
-        if not 0 <= replacement.output_row < token_count:
-            raise IndexError(f"visual output row is out of range: {replacement.output_row}")
-        if not 0 <= replacement.feature_row < sources[k][0].shape[0]:
-            raise IndexError("visual feature row is out of range: "
-                             f"key={replacement.feature_key}, row={replacement.feature_row}")
-        output_rows.append(replacement.output_row)
-        source_index.append(k)
-        feature_rows.append(replacement.feature_row)
+        except (KeyError, TypeError, ValueError) as e:
+            key_error, key_error_at = e, int(first_seen[j])
+            break
+        sources.append((final, deepstack))
+    counts = np.array([f.shape[0] for f, _ in sources] + [np.iinfo(np.int64).max] * (len(key_index) - len(sources)),
+                      dtype=np.int64)
+    bad_out = (out_rows < 0) | (out_rows >= token_count)
+    bad_feat = (feat_rows < 0) | (feat_rows >= counts[source_index])
+    bad = bad_out | bad_feat
+    row_error_at = int(np.argmax(bad)) if bad.any() else n
+    if key_error is not None and key_error_at <= row_error_at:
+        raise key_error
+    if row_error_at < n:
+        r = reps[row_error_at]
+        if bad_out[row_error_at]:
+            raise IndexError(f"visual output row is out of range: {r.output_row}")
+        raise IndexError("visual feature row is out of range: "
+                         f"key={r.feature_key}, row={r.feature_row}")
     layers = layer_count or 0
     if layers > MAX_LAYERS:
         raise NotImplementedError(f"at most {MAX_LAYERS} DeepStack layers are supported, got {layers}")
 
     tokens = _on_device(token_embeddings, device, token_embeddings.dtype)
-    n = len(output_rows)
     table = torch.zeros(len(sources), _TABLE_WORDS, dtype=torch.int64)
     keep = []  # device copies made here stay referenced until the launch is queued
     for k, (final, deepstack) in enumerate(sources):
@@ -123,8 +142,7 @@ def build_planned_visual_embeddings(token_embeddings: torch.Tensor, plan, featur
         for l, d in enumerate(ds):
             table[k, 4 + l] = d.data_ptr()
             table[k, 4 + MAX_LAYERS + l] = d.stride(0) if d.shape[0] > 1 else hidden_size
-    host = torch.cat((torch.tensor(output_rows + source_index + feature_rows, dtype=torch.int64),
-                      table.view(-1)))
+    host = torch.from_numpy(np.concatenate((out_rows, source_index, feat_rows, table.view(-1).numpy())))
     if device.type == "cuda":
         host = host.pin_memory()
     packed = host.to(device, non_blocking=True)

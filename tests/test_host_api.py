@@ -205,3 +205,20 @@ def test_visual_merge_validation_messages_match_reference():
                                deepstack_embeddings=tuple(torch.zeros(2, 4) for _ in range(9)))
     with pytest.raises(NotImplementedError, match="at most 8 DeepStack layers"):
         build(tok, _vm_plan([(0, "a", 0)]), {"a": too_deep})
+
+
+def test_visual_merge_reports_the_first_error_in_plan_order():
+    """The reference validates in one loop over the plan: a key's checks at its first
+    replacement, then that replacement's rows. The vectorised checks raise the same one."""
+    from nano_vllm_multimodal_b200.layers.visual_merge import build_planned_visual_embeddings as build
+
+    tok = torch.zeros(5, 4)
+    feats = {"a": torch.zeros(2, 4)}
+    with pytest.raises(IndexError, match="visual output row is out of range: 9"):
+        build(tok, _vm_plan([(9, "a", 0), (1, "missing", 0)]), feats)
+    with pytest.raises(KeyError, match="missing visual feature: missing"):
+        build(tok, _vm_plan([(1, "missing", 0), (9, "a", 0)]), feats)
+    with pytest.raises(IndexError, match="feature row is out of range: key=a, row=7"):
+        build(tok, _vm_plan([(0, "a", 0), (1, "a", 7), (9, "a", 0)]), feats)
+    with pytest.raises(IndexError, match="visual output row is out of range: -1"):
+        build(tok, _vm_plan([(0, "a", 0), (-1, "a", 7)]), feats)  # output row is checked first
