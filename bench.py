@@ -531,6 +531,49 @@ def visual_merge_component(out, record, flush, seeds, rows, c3):
                                    "reference_torch_ms: the reference's per-key index_select/index_copy_ path")
 
 
+def step_inputs_component(out, device):
+    """Host -> device step inputs of a C3 prefill (32,768 tokens, 16 sequences, 3-axis
+    positions): the reference's one pinned tensor + one copy per array
+    (model_runner.py:700-725,823-870) vs one StepInputStager copy. Host wall time
+    per step (list conversion included), both from the same Python lists."""
+    from nano_vllm_multimodal_b200.step_inputs import StepInputStager
+
+    g = torch.Generator().manual_seed(4242)
+    T, B = 32768, 16
+    ids = torch.randint(0, 151936, (T,), generator=g).tolist()
+    pos = torch.randint(0, 32768, (3, T), generator=g).tolist()
+    cuq = [i * (T // B) for i in range(B + 1)]
+    slots = torch.randperm(1 << 20, generator=g)[:T].int().tolist()
+    ctx = [T // B] * B
+    qs = [0] * B
+    tables = [list(range(i * 8, i * 8 + 8)) for i in range(B)]
+
+    def reference():
+        def cp(v, dt):
+            return torch.tensor(v, dtype=dt, pin_memory=True).cuda(non_blocking=True)
+        return (cp(ids, torch.int64), cp(pos, torch.int64), cp(cuq, torch.int32), cp(cuq, torch.int32),
+                cp(slots, torch.int32), cp(ctx, torch.int32), cp(qs, torch.int32), cp(tables, torch.int32))
+
+    stager = StepInputStager(device=device, slots=3)
+
+    def staged():
+        return stager.prefill_inputs(ids, pos, cuq, cuq, slots, ctx, qs, tables, position_axes=3)
+
+    res = {}
+    for name, fn in (("reference_host_ms", reference), ("staged_host_ms", staged)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(20):
+            fn()
+        res[name] = round((time.perf_counter() - t0) / 20 * 1e3, 3)
+        torch.cuda.synchronize()
+    res.update(copies_reference=8, copies_staged=1, bytes_per_step=T * 8 * 4 + T * 4 + (B + 1) * 8 + B * 8 + B * 8 * 4,
+               config="C3 prefill step inputs: 32,768 tokens, 16 sequences, 3-axis positions")
+    out["step_inputs"] = res
+
+
 def component_bench(inp, device, hbm_peak):
     """The path's kernels that the fused layer does not exercise on their own,
     each at a full config size, timed with CUDA events (working sets > L2)."""
@@ -590,6 +633,7 @@ def component_bench(inp, device, hbm_peak):
     out["add_norm_deepstack"]["unfused"] = "torch add + deepstack_add_ + rms_norm"
     del hs, vis, res
     visual_merge_component(out, record, flush, seeds, rows, c3)
+    step_inputs_component(out, device)
     # generic M-RoPE apply on materialised cos/sin (apply_multimodal_rotary_emb)
     pos = inp["positions"][:, :32768]
     qq = q[:32768]

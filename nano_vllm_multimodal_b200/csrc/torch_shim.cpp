@@ -17,6 +17,8 @@
 #include <torch/custom_class.h>
 #include <torch/library.h>
 
+#include <algorithm>
+#include <cstring>
 #include <deque>
 #include <functional>
 #include <limits>
@@ -613,9 +615,116 @@ class PagedKVCache : public torch::CustomClassHolder {
   std::deque<HostCopy> inflight_;
 };
 
+// A step's host inputs (token ids, positions, slot mapping, cu_seqlens, ...;
+// nanovllm/engine/model_runner.py:700-725,823-870 builds one pinned tensor and
+// one copy per array) staged through ONE pinned buffer and ONE host-to-device
+// copy: stage() writes every CPU tensor into the next slot of a small ring of
+// pinned buffers (16-byte aligned offsets), copies the slot into one fresh
+// device allocation on the current stream and returns typed views of it. A
+// slot is rewritten only after the copy that last read it has completed (its
+// event), so the host can prepare up to `slots` steps ahead.
+class StepInputStager : public torch::CustomClassHolder {
+ public:
+  StepInputStager(int64_t device_index, int64_t slots, int64_t initial_bytes) : device_(device_index) {
+    TORCH_CHECK(device_ >= 0, "CUDA device index must be non-negative");
+    TORCH_CHECK(slots >= 1 && slots <= 64, "StepInputStager: slots must be in [1, 64]");
+    TORCH_CHECK(initial_bytes >= 0, "StepInputStager: initial_bytes must be >= 0");
+    c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device_));
+    ring_.resize(static_cast<size_t>(slots));
+    for (Slot& s : ring_) {
+      NIB_CUDA_CHECK(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+      grow(s, static_cast<size_t>(initial_bytes));
+    }
+  }
+
+  ~StepInputStager() override {
+    c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device_));
+    for (Slot& s : ring_) {
+      if (s.pending) cudaEventSynchronize(s.done);
+      if (s.host) cudaFreeHost(s.host);
+      if (s.done) cudaEventDestroy(s.done);
+    }
+  }
+
+  std::vector<Tensor> stage(std::vector<Tensor> host) {
+    std::vector<size_t> offs;
+    size_t total = 0;
+    for (const Tensor& t : host) {
+      TORCH_CHECK(t.device().is_cpu() && t.is_contiguous(), "StepInputStager: inputs must be contiguous CPU tensors");
+      offs.push_back(total);
+      total += (t.nbytes() + 15u) / 16u * 16u;
+    }
+    c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device_));
+    const auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device_);
+    Tensor dev = at::empty({static_cast<int64_t>(total)}, opts);
+    if (total > 0) {
+      Slot& s = ring_[next_];
+      next_ = (next_ + 1) % ring_.size();
+      if (s.pending) {  // the copy that last read this slot must have landed
+        NIB_CUDA_CHECK(cudaEventSynchronize(s.done));
+        s.pending = false;
+      }
+      grow(s, total);
+      for (size_t i = 0; i < host.size(); ++i)
+        if (host[i].nbytes()) std::memcpy(static_cast<char*>(s.host) + offs[i], host[i].data_ptr(), host[i].nbytes());
+      cudaStream_t st = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(device_)).stream();
+      NIB_CUDA_CHECK(cudaMemcpyAsync(dev.data_ptr(), s.host, total, cudaMemcpyHostToDevice, st));
+      NIB_CUDA_CHECK(cudaEventRecord(s.done, st));
+      s.pending = true;
+    }
+    std::vector<Tensor> out;
+    out.reserve(host.size());
+    for (size_t i = 0; i < host.size(); ++i) {
+      const Tensor& t = host[i];
+      Tensor v = dev.narrow(0, static_cast<int64_t>(offs[i]), static_cast<int64_t>(t.nbytes()));
+      out.push_back(v.view(t.scalar_type()).view(t.sizes()));
+    }
+    return out;
+  }
+
+  int64_t slots() const { return static_cast<int64_t>(ring_.size()); }
+  int64_t slot_bytes(int64_t i) const {
+    TORCH_CHECK(i >= 0 && i < slots(), "StepInputStager: slot index out of range");
+    return static_cast<int64_t>(ring_[static_cast<size_t>(i)].bytes);
+  }
+
+ private:
+  struct Slot {
+    void* host = nullptr;
+    size_t bytes = 0;
+    cudaEvent_t done = nullptr;
+    bool pending = false;
+  };
+
+  static void grow(Slot& s, size_t bytes) {
+    if (s.bytes >= bytes) return;
+    const size_t want = std::max<size_t>(bytes, 2 * s.bytes);  // amortised growth
+    if (s.pending) {
+      NIB_CUDA_CHECK(cudaEventSynchronize(s.done));
+      s.pending = false;
+    }
+    if (s.host) NIB_CUDA_CHECK(cudaFreeHost(s.host));
+    s.host = nullptr;
+    s.bytes = 0;
+    NIB_CUDA_CHECK(cudaHostAlloc(&s.host, want, cudaHostAllocDefault));
+    s.bytes = want;
+  }
+
+  int64_t device_;
+  std::vector<Slot> ring_;
+  size_t next_ = 0;
+};
+
 int64_t abi_version() { return nib_abi_version(); }
 
 }  // namespace nib_torch
+
+static auto step_input_stager_class =
+    torch::class_<nib_torch::StepInputStager>("nanoinfer_b200", "StepInputStager")
+        .def(torch::init<int64_t, int64_t, int64_t>())
+        .def("stage", &nib_torch::StepInputStager::stage)
+        .def("slots", &nib_torch::StepInputStager::slots)
+        .def("slot_bytes", &nib_torch::StepInputStager::slot_bytes);
 
 static auto paged_kv_cache_class =
     torch::class_<nib_torch::PagedKVCache>("nanovllm_paged_kv", "PagedKVCache")
