@@ -74,6 +74,10 @@ def parse_args(argv=None):
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-components", action="store_true", help="skip the per-kernel extras")
+    p.add_argument("--component", choices=("decode_attention", "step_inputs"), default=None,
+                   help="run only this standalone component (one GPU) and print its JSON")
+    p.add_argument("--decode-requests", type=int, default=256,
+                   help="requests of the decode-attention component (C2: 256)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     p.add_argument("--cache-blocks", type=int, default=CACHE_BLOCKS,
                    help="blocks of 256 slots per K/V cache per GPU (smaller only for profiler captures)")
@@ -574,6 +578,50 @@ def step_inputs_component(out, device):
     out["step_inputs"] = res
 
 
+def decode_attention_component(out, record, flush, device, requests=256):
+    """Paged decode attention at C2 decode: 256 requests, 16/8 heads of 128, 256-token
+    blocks, contexts U[1, 8192] (C2 positions U[0, 8191] plus the new token); the kernel
+    against the roofline, and flash-attn's own flash_attn_with_kvcache (the reference's
+    decode kernel) on the same inputs when it runs on this GPU."""
+    from nano_vllm_multimodal_b200 import ops
+
+    g = torch.Generator().manual_seed(5151)
+    B, NQ_, NKV_, D_, BS_ = requests, 16, 8, 128, 256
+    lens = torch.randint(1, 8193, (B,), generator=g, dtype=torch.int32)
+    need = (lens + BS_ - 1) // BS_
+    nblocks = int(need.sum()) + 16
+    width = int(need.max())
+    perm = torch.randperm(nblocks, generator=g).to(torch.int32)
+    tables = torch.full((B, width), 0, dtype=torch.int32)
+    at = 0
+    for b in range(B):
+        n = int(need[b])
+        tables[b, :n] = perm[at:at + n]
+        at += n
+    kc = torch.randn(nblocks, BS_, NKV_, D_, device=device, dtype=torch.bfloat16)
+    vc = torch.randn(nblocks, BS_, NKV_, D_, device=device, dtype=torch.bfloat16)
+    q = torch.randn(B, NQ_, D_, device=device, dtype=torch.bfloat16)
+    cl, tb = lens.to(device), tables.to(device)
+    scale = D_ ** -0.5
+    ms = _time_op(flush=flush, fn=lambda: ops.decode_attention(q, kc, vc, cl, tb, scale, 8192))
+    nbytes = int(lens.sum()) * NKV_ * D_ * 2 * 2 + B * NQ_ * D_ * 2 * 2 + B * 4 + int(need.sum()) * 4
+    record("decode_attention", ms, nbytes,
+           f"C2 decode: {B} requests, 16/8 heads x 128, 256-token blocks, contexts U[1,8192]")
+    try:
+        from flash_attn import flash_attn_with_kvcache as fa
+
+        ref = fa(q.unsqueeze(1), kc, vc, cache_seqlens=cl, block_table=tb, softmax_scale=scale, causal=True)
+        mine = ops.decode_attention(q, kc, vc, cl, tb, scale, 8192)
+        diff = float((ref[:, 0].float() - mine.float()).abs().max())
+        ms_fa = _time_op(flush=flush, fn=lambda: fa(q.unsqueeze(1), kc, vc, cache_seqlens=cl, block_table=tb,
+                                                    softmax_scale=scale, causal=True))
+        out["decode_attention"]["flash_attn_ms"] = round(ms_fa, 4)
+        out["decode_attention"]["max_abs_diff_vs_flash_attn"] = round(diff, 5)
+    except Exception as e:  # the library may carry no kernels for this GPU
+        out["decode_attention"]["flash_attn"] = f"unavailable: {type(e).__name__}: {str(e)[:120]}"
+    del kc, vc
+
+
 def component_bench(inp, device, hbm_peak):
     """The path's kernels that the fused layer does not exercise on their own,
     each at a full config size, timed with CUDA events (working sets > L2)."""
@@ -634,6 +682,7 @@ def component_bench(inp, device, hbm_peak):
     del hs, vis, res
     visual_merge_component(out, record, flush, seeds, rows, c3)
     step_inputs_component(out, device)
+    decode_attention_component(out, record, flush, device)
     # generic M-RoPE apply on materialised cos/sin (apply_multimodal_rotary_emb)
     pos = inp["positions"][:, :32768]
     qq = q[:32768]
@@ -778,13 +827,7 @@ def ours_arm(args, rank, world, local):
     step_bytes_job = max_over_ranks(float(step_bytes), world, device) * world
 
     # ---- per-kernel roofline (this rank's launches)
-    peaks = {}
-    pk = ROOT / "MEASURED_PEAKS.json"
-    if pk.exists():
-        peaks = json.loads(pk.read_text())
-    hbm_peak = peaks.get("hbm_gbs")
-    peak_src = "measured" if hbm_peak else "fallback"
-    hbm_peak = hbm_peak or 6650.0
+    hbm_peak, peak_src = measured_hbm_peak(with_source=True)
     traffic_tbl = load_traffic_table()
     per_kernel = {}
     for name, s in kernels.items():
@@ -859,11 +902,48 @@ def ours_arm(args, rank, world, local):
     return 0
 
 
+def measured_hbm_peak(with_source=False):
+    """HBM copy bandwidth (GB/s) from MEASURED_PEAKS.json, else the pool's fallback figure."""
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    peak = peaks.get("hbm_gbs")
+    src = "measured" if peak else "fallback"
+    peak = peak or 6650.0
+    return (peak, src) if with_source else peak
+
+
+def component_only(name, decode_requests=256):
+    """One standalone component on cuda:0 (for profiling a single kernel)."""
+    from nano_vllm_multimodal_b200 import ops  # noqa: F401  (loads the extension, fails loudly)
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    hbm_peak = measured_hbm_peak()
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=device)
+    out = {}
+
+    def record(n, ms, nbytes, cfg):
+        gbs = nbytes / (ms / 1000.0) / 1e9
+        out[n] = {"avg_ms": round(ms, 4), "bytes": int(nbytes), "achieved_gbs": round(gbs, 1),
+                  "frac": round(gbs / hbm_peak, 4), "config": cfg}
+
+    if name == "decode_attention":
+        decode_attention_component(out, record, flush, device, decode_requests)
+    else:
+        step_inputs_component(out, device)
+    print(json.dumps({"component": name, "peak_gbs": hbm_peak, **out}))
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     rank, world, local = dist_env()
     if args.impl == "reference":
         return reference_arm(args, rank, world)
+    if args.component is not None:
+        return component_only(args.component, args.decode_requests)
     if world != args.gpus and world == 1 and args.gpus > 1:
         print(f"bench.py: --gpus {args.gpus} needs torchrun with {args.gpus} processes", file=sys.stderr)
         return 2

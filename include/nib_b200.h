@@ -136,6 +136,51 @@ NIB_API int nib_visual_merge(int dtype, const void* token_embeddings, int64_t to
                      int64_t num_replacements, int32_t* row_map, void* merged,
                      void* deepstack_out, unsigned int* status, void* stream);
 
+/* ------------------------------------------------------------------ decode attention */
+
+/* Paged decode attention: out[b, h] = softmax(q[b, h] . K^T * scale) V over the
+ * first context_lens[b] tokens of request b's cache, token t at slot
+ * t % block_size of block block_tables[b, t / block_size]; q head h reads kv
+ * head h / (num_heads / num_kv_heads). Caches are [num_blocks, block_size,
+ * num_kv_heads, head_dim] with the given strides (elements). dtype bf16 or
+ * f16, head_dim 64 / 128 / 256, at most 16 q heads per kv head; arithmetic in
+ * fp32, output rounded once. A context length outside [0, max_blocks_per_seq *
+ * block_size] sets NIB_DEV_BAD_INDEX and is clamped; a block id outside
+ * [0, num_blocks) sets NIB_DEV_BAD_BLOCK and its token is left out. An empty
+ * context gives zeros. max_context_len (host upper bound, 0 = from the table
+ * width) picks how many CTAs split a context; the partials then need
+ * nib_decode_attention_workspace_bytes() bytes of device workspace.
+ * Replaces: flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
+ * cache_seqlens, block_table, softmax_scale, causal=True)
+ * nanovllm/layers/attention.py:122-130 (numerics: the SDPA decode branch,
+ * attention.py:286-300) */
+typedef struct nib_decode_attention_args {
+  int32_t struct_size; /* sizeof(nib_decode_attention_args) */
+  int32_t dtype;
+  int64_t batch;
+  int32_t num_heads, num_kv_heads, head_dim, reserved;
+  const void* q;
+  int64_t q_batch_stride, q_head_stride;
+  const void* key_cache;
+  const void* value_cache;
+  int64_t cache_block_stride, cache_slot_stride, cache_head_stride;
+  int64_t num_blocks, block_size;
+  const int32_t* block_tables;
+  int64_t block_table_stride, max_blocks_per_seq;
+  const int32_t* context_lens;
+  float scale;
+  int32_t reserved2;
+  void* out;
+  int64_t out_batch_stride, out_head_stride;
+  void* workspace;
+  int64_t workspace_bytes;
+  int64_t max_context_len;
+  unsigned int* status;
+} nib_decode_attention_args;
+
+NIB_API int64_t nib_decode_attention_workspace_bytes(const nib_decode_attention_args* args);
+NIB_API int nib_decode_attention(const nib_decode_attention_args* args, void* stream);
+
 /* ------------------------------------------------------------------ activation */
 
 /* y[t, :] = silu(x[t, :I]) * x[t, I:2I], computed in fp32, rounded once.

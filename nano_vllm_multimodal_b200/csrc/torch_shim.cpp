@@ -412,6 +412,69 @@ void deepstack_add_(Tensor hidden, const Tensor& rows, const Tensor& vis, const 
         "nanoinfer_b200::deepstack_add_");
 }
 
+Tensor decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache,
+                        const Tensor& context_lens, const Tensor& block_tables, double scale,
+                        int64_t max_context_len, const optional<Tensor>& status) {
+  TORCH_CHECK(q.dim() == 3 && q.stride(2) == 1, "decode_attention: q must be [batch, heads, head_dim]");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes() && k_cache.stride(3) == 1 &&
+                  v_cache.strides() == k_cache.strides(),
+              "decode_attention: caches must be [blocks, block_size, kv_heads, head_dim] of one layout");
+  TORCH_CHECK(q.scalar_type() == k_cache.scalar_type() && v_cache.scalar_type() == q.scalar_type(),
+              "decode_attention: q and caches must share a dtype");
+  TORCH_CHECK(q.size(2) == k_cache.size(3), "decode_attention: head_dim mismatch");
+  TORCH_CHECK(context_lens.scalar_type() == at::kInt && context_lens.dim() == 1 && context_lens.size(0) == q.size(0),
+              "decode_attention: context_lens must be int32 [batch]");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2 &&
+                  block_tables.size(0) == q.size(0) && block_tables.stride(1) == 1,
+              "decode_attention: block_tables must be int32 [batch, max_blocks]");
+  on_device(q, k_cache, "decode_attention key cache");
+  on_device(q, v_cache, "decode_attention value cache");
+  on_device(q, context_lens, "decode_attention context_lens");
+  on_device(q, block_tables, "decode_attention block_tables");
+  c10::cuda::CUDAGuard guard(q.device());
+  Tensor out = at::empty(q.sizes(), q.options().memory_format(at::MemoryFormat::Contiguous));
+  if (q.size(0) == 0) return out;
+  Tensor lens = context_lens.contiguous();
+  nib_decode_attention_args a{};
+  a.struct_size = sizeof(a);
+  a.dtype = code_of(q.scalar_type());
+  a.batch = q.size(0);
+  a.num_heads = static_cast<int32_t>(q.size(1));
+  a.num_kv_heads = static_cast<int32_t>(k_cache.size(2));
+  a.head_dim = static_cast<int32_t>(q.size(2));
+  a.q = q.data_ptr();
+  a.q_batch_stride = q.stride(0);
+  a.q_head_stride = q.stride(1);
+  a.key_cache = k_cache.data_ptr();
+  a.value_cache = v_cache.data_ptr();
+  a.cache_block_stride = k_cache.stride(0);
+  a.cache_slot_stride = k_cache.stride(1);
+  a.cache_head_stride = k_cache.stride(2);
+  a.num_blocks = k_cache.size(0);
+  a.block_size = k_cache.size(1);
+  a.block_tables = block_tables.data_ptr<int32_t>();
+  a.block_table_stride = block_tables.stride(0);
+  a.max_blocks_per_seq = block_tables.size(1);
+  a.context_lens = lens.data_ptr<int32_t>();
+  a.scale = static_cast<float>(scale);
+  a.out = out.data_ptr();
+  a.out_batch_stride = out.stride(0);
+  a.out_head_stride = out.stride(1);
+  a.max_context_len = max_context_len;
+  a.status = status_ptr(status);
+  const int64_t need = nib_decode_attention_workspace_bytes(&a);
+  TORCH_CHECK(need >= 0, "decode_attention: unsupported configuration (head_dim ", a.head_dim, ", heads ",
+              a.num_heads, "/", a.num_kv_heads, ", dtype ", q.scalar_type(), ")");
+  Tensor ws;
+  if (need > 0) {
+    ws = at::empty({need}, q.options().dtype(at::kByte));
+    a.workspace = ws.data_ptr();
+    a.workspace_bytes = need;
+  }
+  check(nib_decode_attention(&a, stream_of(q)), "nanoinfer_b200::decode_attention");
+  return out;
+}
+
 Tensor deepstack_row_index(const Tensor& rows, int64_t tokens, const optional<Tensor>& status) {
   TORCH_CHECK(rows.scalar_type() == at::kLong && rows.dim() == 1, "deepstack_row_index: rows must be int64 [n]");
   TORCH_CHECK(tokens >= 0, "deepstack_row_index: tokens must be >= 0");
@@ -761,6 +824,8 @@ TORCH_LIBRARY(nanoinfer_b200, m) {
         "Tensor(a!)? status) -> Tensor");
   m.def("deepstack_add(Tensor hidden, Tensor rows, Tensor vis, Tensor(a!)? status) -> Tensor");
   m.def("deepstack_row_index(Tensor rows, int tokens, Tensor(a!)? status) -> Tensor");
+  m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor context_lens, Tensor block_tables, "
+        "float scale, int max_context_len, Tensor(a!)? status) -> Tensor");
   m.def("visual_merge(Tensor tokens, Tensor table, int num_layers, Tensor plan, int num_replacements, "
         "Tensor(a!)? status) -> (Tensor, Tensor)");
   m.def("add_rms_norm_deepstack(Tensor x, Tensor residual, Tensor weight, float eps, Tensor vis, "
@@ -780,6 +845,7 @@ TORCH_LIBRARY_IMPL(nanoinfer_b200, CUDA, m) {
   m.impl("deepstack_add", TORCH_FN(nib_torch::deepstack_add));
   m.impl("deepstack_add_", TORCH_FN(nib_torch::deepstack_add_));
   m.impl("deepstack_row_index", TORCH_FN(nib_torch::deepstack_row_index));
+  m.impl("decode_attention", TORCH_FN(nib_torch::decode_attention));
   m.impl("visual_merge", TORCH_FN(nib_torch::visual_merge));
   m.impl("add_rms_norm_deepstack", TORCH_FN(nib_torch::add_rms_norm_deepstack));
 }

@@ -9,7 +9,9 @@ hot-path names that the decoder models import at module load:
 * ``nanovllm.layers.multimodal_rotary_embedding.{MultimodalRotaryEmbedding,
   apply_multimodal_rotary_emb}``
 * ``nanovllm.layers.embed_head.VocabParallelEmbedding``
-* ``nanovllm.layers.attention.store_kvcache``
+* ``nanovllm.layers.attention.{store_kvcache, flash_attn_with_kvcache}`` (the
+  decode attention reads the paged cache with this package's kernel; prefill
+  keeps ``flash_attn_varlen_func``)
 * ``nanovllm.models.qwen3_vl.Qwen3VLTextRMSNorm`` and
   ``Qwen3VLLanguageModel._add_deepstack_rows``
 * ``nanovllm.engine.model_runner.{build_planned_visual_embeddings,
@@ -60,7 +62,8 @@ def _targets():
             "MultimodalRotaryEmbedding": mrope.MultimodalRotaryEmbedding,
             "apply_multimodal_rotary_emb": mrope.apply_multimodal_rotary_emb},
         "nanovllm.layers.embed_head": {"VocabParallelEmbedding": embed_head.VocabParallelEmbedding},
-        "nanovllm.layers.attention": {"store_kvcache": attention.store_kvcache},
+        "nanovllm.layers.attention": {"store_kvcache": attention.store_kvcache,
+                                      "flash_attn_with_kvcache": attention.flash_attn_with_kvcache},
         "nanovllm.layers.paged_kv.loader": {"load_paged_kv_extension": load_paged_kv_extension},
         "nanovllm.layers.paged_kv.cuda_backend": {"load_paged_kv_extension": load_paged_kv_extension},
         "nanovllm.models.qwen3_vl": {"Qwen3VLTextRMSNorm": qwen3_vl.Qwen3VLTextRMSNorm},

@@ -1,5 +1,5 @@
-"""Attention-side pieces of the hot path: the paged KV store and the fused
-attention prologue.
+"""Attention-side pieces of the hot path: the paged KV store, the fused
+attention prologue and the paged decode attention that reads the cache.
 
 ``store_kvcache`` keeps the signature of ``nanovllm/layers/attention.py:10-33``.
 ``attention_prologue`` replaces, in one kernel launch, the sequence the
@@ -77,3 +77,59 @@ def attention_prologue(qkv: torch.Tensor, *, num_heads: int, num_kv_heads: int, 
         cache = dict(v=v, key_cache=k_cache, value_cache=v_cache, slot_mapping=slot_mapping)
     q_rot, k_rot = ops.qk_prologue(q, k, positions=positions, **norm, **_rope_args(rotary_emb), **cache)
     return q_rot, k_rot, v
+
+
+def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                           context_lens: torch.Tensor, block_tables: torch.Tensor, scale: float,
+                           max_context_len: int = 0) -> torch.Tensor:
+    """One query token per request against its paged cache -> ``[batch, heads, head_dim]``
+    (the reference's SDPA decode branch, ``nanovllm/layers/attention.py:286-300``)."""
+    if context_lens.dtype != torch.int32:
+        context_lens = context_lens.to(torch.int32)
+    if block_tables.dtype != torch.int32:
+        block_tables = block_tables.to(torch.int32)
+    return ops.decode_attention(q, k_cache, v_cache, context_lens, block_tables, scale, max_context_len)
+
+
+_FA_DEFAULTS = {"softcap": 0.0, "rotary_interleaved": True, "return_softmax_lse": False}
+
+
+def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None, rotary_sin=None,
+                            cache_seqlens=None, cache_batch_idx=None, cache_leftpad=None,
+                            block_table=None, softmax_scale=None, causal=False, **kwargs):
+    """Drop-in for the decode call ``flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
+    cache_seqlens=..., block_table=..., softmax_scale=..., causal=True)``
+    (``nanovllm/layers/attention.py:122-130``): q ``[batch, 1, heads, head_dim]`` ->
+    ``[batch, 1, heads, head_dim]``. With one query token per request, causal and
+    non-causal attention are the same. Features that call does not use (appending
+    k/v, rotary, batch indices, left padding, windows, softcap, ...) are refused."""
+    unused = dict(k=k, v=v, rotary_cos=rotary_cos, rotary_sin=rotary_sin,
+                  cache_batch_idx=cache_batch_idx, cache_leftpad=cache_leftpad)
+    given = [name for name, val in unused.items() if val is not None]
+    for name, val in kwargs.items():
+        if name == "num_splits":  # a scheduling hint of flash-attn; the split count is chosen here
+            continue
+        if name == "window_size":
+            if tuple(val) != (-1, -1):
+                given.append(name)
+        elif name == "alibi_slopes":
+            if val is not None:
+                given.append(name)
+        elif name in _FA_DEFAULTS:
+            if val != _FA_DEFAULTS[name]:
+                given.append(name)
+        else:
+            given.append(name)
+    if given:
+        raise NotImplementedError(f"flash_attn_with_kvcache: unsupported arguments {given}")
+    if q.dim() != 4 or q.shape[1] != 1:
+        raise NotImplementedError("flash_attn_with_kvcache: one query token per request is supported")
+    if cache_seqlens is None or block_table is None:
+        raise NotImplementedError("flash_attn_with_kvcache: a paged cache (block_table, cache_seqlens) is required")
+    scale = softmax_scale if softmax_scale is not None else q.shape[-1] ** -0.5
+    lens = cache_seqlens
+    if isinstance(lens, int):
+        lens = torch.full((q.shape[0],), lens, dtype=torch.int32, device=q.device)
+    out = paged_decode_attention(q[:, 0], k_cache, v_cache, lens, block_table, scale,
+                                 block_table.shape[1] * k_cache.shape[1])
+    return out.unsqueeze(1)

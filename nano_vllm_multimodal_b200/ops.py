@@ -224,6 +224,18 @@ def visual_merge(token_embeddings, table, num_layers: int, plan, num_replacement
     return out
 
 
+def decode_attention(q, k_cache, v_cache, context_lens, block_tables, scale: float,
+                     max_context_len: int = 0) -> torch.Tensor:
+    """Paged decode attention -> ``[batch, heads, head_dim]`` (``nib_decode_attention``).
+    ``max_context_len`` is an optional host upper bound of ``context_lens`` (0: the
+    block-table width times the block size); it only chooses how a context is split."""
+    st = _status_for(q)
+    out = _ops().decode_attention(q, k_cache, v_cache, context_lens, block_tables, float(scale),
+                                  int(max_context_len), st)
+    _check_status(st, "decode_attention")
+    return out
+
+
 def deepstack_row_index(rows, tokens: int) -> torch.Tensor:
     """int32 ``[tokens]``: ``j`` at ``rows[j]``, ``-1`` elsewhere (the map the
     folded add + norm + DeepStack kernel reads; build once per forward)."""

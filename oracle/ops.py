@@ -24,6 +24,7 @@ __all__ = [
     "add_text_rms_norm",
     "add_text_rms_norm_deepstack",
     "planned_visual_embeddings",
+    "paged_decode_attention",
     "silu_and_mul",
     "silu_and_mul_fp32",
     "rope_cos_sin_cache",
@@ -392,6 +393,31 @@ def paged_gather(cache, block_table, sequence_length):
     ids = block_table.numpy()[:req].astype(np.int64)
     rows = c[ids].reshape(req * bs, h, d)[:sequence_length]
     return _from_int_view(rows, cache.dtype)
+
+
+def paged_decode_attention(q, k_cache, v_cache, context_lens, block_tables, scale):
+    """Decode attention over a paged cache, the reference's SDPA decode branch
+    (``nanovllm/layers/attention.py:286-300``; gather ``:163-178``, SDPA with
+    grouped-query heads ``:180-204``) evaluated in float64.
+
+    Per request ``b``: K, V = the first ``context_lens[b]`` cached tokens
+    (``paged_gather``); q head ``h`` uses kv head ``h // (heads / kv_heads)``;
+    ``out = softmax(q . K^T * scale) V`` rounded once to q's dtype. An empty
+    context gives zeros. q is ``[batch, heads, head_dim]``.
+    """
+    batch, heads, dim = q.shape
+    group = heads // k_cache.shape[2]
+    out = torch.zeros(batch, heads, dim, dtype=q.dtype)
+    for b in range(batch):
+        n = int(context_lens[b])
+        if n == 0:
+            continue
+        k = paged_gather(k_cache, block_tables[b], n).double()
+        v = paged_gather(v_cache, block_tables[b], n).double()
+        for h in range(heads):
+            p = torch.softmax((k[:, h // group] @ q[b, h].double()) * scale, dim=0)
+            out[b, h] = (p @ v[:, h // group]).to(q.dtype)
+    return out
 
 
 def embedding(ids, weight):

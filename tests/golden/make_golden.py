@@ -51,6 +51,8 @@ SOURCES = [
     "nanovllm/models/qwen25_vl.py",
     "nanovllm/engine/model_runner.py",
     "nanovllm/multimodal/runtime.py",
+    "nanovllm/layers/attention.py",
+    "nanovllm/utils/context.py",
 ]
 
 
@@ -65,6 +67,8 @@ def _ref():
         VisualReplacement, VisualReplacementPlan, build_planned_visual_embeddings)
     from nanovllm.models.qwen3_vl import Qwen3VLLanguageModel, Qwen3VLTextRMSNorm
     from nanovllm.multimodal.runtime import VisionFeatureBundle
+    from nanovllm.layers.attention import SDPAAttention
+    from nanovllm.utils.context import reset_context, set_context
     with patch("torch.distributed.get_rank", return_value=0), \
             patch("torch.distributed.get_world_size", return_value=1):
         from nanovllm.layers.embed_head import VocabParallelEmbedding
@@ -74,7 +78,8 @@ def _ref():
                 add_deepstack=Qwen3VLLanguageModel._add_deepstack_rows,
                 Embedding=VocabParallelEmbedding, VisualReplacement=VisualReplacement,
                 VisualReplacementPlan=VisualReplacementPlan, Bundle=VisionFeatureBundle,
-                build_visual=build_planned_visual_embeddings)
+                build_visual=build_planned_visual_embeddings, SDPA=SDPAAttention,
+                set_context=set_context, reset_context=reset_context)
 
 
 def _rms(R, hidden, weight, eps=1e-6):
@@ -239,6 +244,27 @@ def build():
         outputs=dict(final_embedding=vm.final_embedding, deepstack=torch.stack(vm.deepstack_embeddings),
                      visual_rows=vm.visual_rows),
         meta=dict(keys=keys))
+
+    # ---- (f) paged decode attention: the reference's SDPA decode branch (the numerical
+    # reference of flash_attn_with_kvcache), GQA 16/8, head_dim 128, 16-token blocks,
+    # ragged contexts incl. a one-token context, non-sequential block tables
+    g = torch.Generator().manual_seed(3300)
+    B, NQ_, NKV_, D_, BS_, NB_ = 6, 16, 8, 128, 16, 24
+    kc = torch.randn(NB_, BS_, NKV_, D_, generator=g).to(torch.bfloat16)
+    vc = torch.randn(NB_, BS_, NKV_, D_, generator=g).to(torch.bfloat16)
+    lens = torch.tensor([1, 17, 40, 5, 64, 33], dtype=torch.int32)
+    tables = torch.stack([torch.randperm(NB_, generator=g)[:4] for _ in range(B)]).to(torch.int32)
+    qd = torch.randn(B, NQ_, D_, generator=g).to(torch.bfloat16)
+    attn = R["SDPA"](NQ_, D_, D_ ** -0.5, NKV_)
+    attn.k_cache, attn.v_cache = kc, vc
+    attn.paged_kv_backend = R["Store"]()
+    R["set_context"](False, slot_mapping=torch.full((B,), -1, dtype=torch.int32), context_lens=lens,
+                     block_tables=tables)
+    od = attn(qd, torch.zeros(B, NKV_, D_, dtype=torch.bfloat16), torch.zeros(B, NKV_, D_, dtype=torch.bfloat16))
+    R["reset_context"]()
+    cases["decode_attention_c2"] = dict(
+        inputs=dict(q=qd, k_cache=kc, v_cache=vc, context_lens=lens, block_tables=tables),
+        outputs=dict(out=od), meta=dict(scale=D_ ** -0.5))
 
     # ---- a8: fused attention prologues, composed from the reference modules
     def fused(dd, shape, norm_mod, rope_fn, slots_seed, skip):

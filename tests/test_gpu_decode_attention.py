@@ -1,0 +1,106 @@
+"""Paged decode attention (``nib_decode_attention``) against the oracle and the reference.
+
+Tolerances (attention is floating point; the kernel computes in fp32):
+* against the float64 oracle: |out - oracle| <= 2^-8 * |oracle| + 1e-4, i.e. one
+  bf16/fp16 rounding plus a floor for outputs that nearly cancel;
+* against the reference's own SDPA decode output (golden fixture, CPU bf16):
+  |out - reference| <= 2^-6 * max(1, |reference|), the bound the oracle meets.
+"""
+
+import pytest
+import torch
+
+import oracle as O
+from nano_vllm_multimodal_b200 import ops
+from nano_vllm_multimodal_b200.layers.attention import flash_attn_with_kvcache, paged_decode_attention
+
+pytestmark = pytest.mark.gpu
+
+
+def _close_to_oracle(out, expect, what):
+    o, e = out.detach().cpu().double(), expect.double()
+    bad = (o - e).abs() > 2.0 ** -8 * e.abs() + 1e-4
+    assert not bool(bad.any()), f"{what}: {int(bad.sum())} elements off, max {float((o - e).abs().max()):.3g}"
+
+
+def test_golden_reference_case(golden):
+    c = golden["decode_attention_c2"]
+    i = c["inputs"]
+    out = paged_decode_attention(i["q"].cuda(), i["k_cache"].cuda(), i["v_cache"].cuda(),
+                                 i["context_lens"].cuda(), i["block_tables"].cuda(), c["meta"]["scale"])
+    ref = c["outputs"]["out"].double()
+    assert bool(((out.cpu().double() - ref).abs() <= 2.0 ** -6 * ref.abs().clamp(min=1.0)).all())
+    _close_to_oracle(out, O.paged_decode_attention(i["q"], i["k_cache"], i["v_cache"], i["context_lens"],
+                                                   i["block_tables"], c["meta"]["scale"]), "golden")
+
+
+def _case(seed, batch, nq, nkv, dim, bs, lens, nblocks=None, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    need = [max(1, -(-n // bs)) for n in lens]
+    nblocks = nblocks or sum(need) + 3
+    kc = torch.randn(nblocks, bs, nkv, dim, generator=g).to(dtype)
+    vc = torch.randn(nblocks, bs, nkv, dim, generator=g).to(dtype)
+    width = max(need)
+    perm = torch.randperm(nblocks, generator=g)
+    tables = torch.full((batch, width), -1, dtype=torch.int32)
+    at = 0
+    for b, n in enumerate(need):
+        tables[b, :n] = perm[at:at + n].to(torch.int32)
+        at += n
+    q = torch.randn(batch, nq, dim, generator=g).to(dtype)
+    return q, kc, vc, torch.tensor(lens, dtype=torch.int32), tables
+
+
+@pytest.mark.parametrize("nq,nkv,dim,bs,lens", [
+    (16, 8, 128, 256, [1, 255, 256, 257, 1000, 3]),       # Qwen3 GQA, 256-token blocks
+    (16, 2, 128, 16, [7, 64, 300, 33]),                   # Qwen2.5-VL GQA 8, small blocks
+    (14, 2, 64, 24, [50, 1, 97]),                         # 7 heads per kv head, non-power-of-2 blocks
+    (8, 8, 256, 32, [0, 40, 129]),                        # MHA, head_dim 256, an empty context
+])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_matches_oracle(nq, nkv, dim, bs, lens, dtype):
+    q, kc, vc, cl, tb = _case(nq * 1000 + dim + bs, len(lens), nq, nkv, dim, bs, lens, dtype=dtype)
+    scale = dim ** -0.5
+    out = paged_decode_attention(q.cuda(), kc.cuda(), vc.cuda(), cl.cuda(), tb.cuda(), scale)
+    _close_to_oracle(out, O.paged_decode_attention(q, kc, vc, cl, tb, scale), f"{nq}/{nkv} D{dim} bs{bs}")
+    if 0 in lens:
+        assert not out[lens.index(0)].any()
+
+
+def test_long_contexts_split_across_ctas_and_strided_q():
+    """Few requests with long contexts take several CTAs per (request, kv head) and a
+    combine pass; q is a strided view (a slice of a fused qkv row)."""
+    q, kc, vc, cl, tb = _case(77, 2, 16, 8, 128, 256, [20000, 9000])
+    qkv = torch.randn(2, (16 + 16) * 128).to(torch.bfloat16)
+    qkv[:, :2048] = q.reshape(2, -1)
+    qv = qkv.cuda()[:, :2048].view(2, 16, 128)
+    assert qv.stride(0) == 32 * 128
+    out = paged_decode_attention(qv, kc.cuda(), vc.cuda(), cl.cuda(), tb.cuda(), 128 ** -0.5)
+    _close_to_oracle(out, O.paged_decode_attention(q, kc, vc, cl, tb, 128 ** -0.5), "split contexts")
+
+
+def test_flash_attn_shaped_drop_in():
+    q, kc, vc, cl, tb = _case(5, 4, 16, 8, 128, 256, [3, 700, 256, 1])
+    qg, kg, vg, cg, tg = q.cuda(), kc.cuda(), vc.cuda(), cl.cuda(), tb.cuda()
+    o = flash_attn_with_kvcache(qg.unsqueeze(1), kg, vg, cache_seqlens=cg, block_table=tg,
+                                softmax_scale=128 ** -0.5, causal=True)
+    assert o.shape == (4, 1, 16, 128)
+    assert torch.equal(o[:, 0], paged_decode_attention(qg, kg, vg, cg, tg, 128 ** -0.5))
+    with pytest.raises(NotImplementedError, match="one query token"):
+        flash_attn_with_kvcache(torch.cat((qg.unsqueeze(1), qg.unsqueeze(1)), 1), kg, vg,
+                                cache_seqlens=cg, block_table=tg)
+    with pytest.raises(NotImplementedError, match="unsupported arguments"):
+        flash_attn_with_kvcache(qg.unsqueeze(1), kg, vg, cache_seqlens=cg, block_table=tg, softcap=30.0)
+
+
+def test_bad_block_and_length_reported(monkeypatch):
+    monkeypatch.setenv("NANOINFER_B200_VALIDATE", "1")
+    q, kc, vc, cl, tb = _case(9, 2, 16, 8, 128, 16, [20, 5])
+    bad = tb.clone()
+    bad[0, 1] = 999
+    with pytest.raises(ValueError, match="block"):
+        ops.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), cl.cuda(), bad.cuda(), 0.1)
+    long = cl.clone()
+    long[1] = 10_000
+    with pytest.raises(ValueError, match="out of range"):
+        ops.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), long.cuda(), tb.cuda(), 0.1)

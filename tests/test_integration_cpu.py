@@ -22,7 +22,7 @@ def fake_nanovllm(tmp_path, monkeypatch):
         "nanovllm/layers/multimodal_rotary_embedding.py": "class MultimodalRotaryEmbedding: pass\n"
                                                           "def apply_multimodal_rotary_emb(*a): pass\n",
         "nanovllm/layers/embed_head.py": "class VocabParallelEmbedding: pass\n",
-        "nanovllm/layers/attention.py": "def store_kvcache(*a): pass\n",
+        "nanovllm/layers/attention.py": "def store_kvcache(*a): pass\ndef flash_attn_with_kvcache(*a, **k): pass\n",
         "nanovllm/layers/paged_kv/__init__.py": "",
         "nanovllm/layers/paged_kv/loader.py": "def load_paged_kv_extension(*, verbose=False): raise RuntimeError('jit')\n",
         "nanovllm/layers/paged_kv/cuda_backend.py": "from nanovllm.layers.paged_kv.loader import load_paged_kv_extension\n",
@@ -85,6 +85,9 @@ def test_install_rebinds_hot_path_names(fake_nanovllm):
     import torch
     from types import SimpleNamespace
     assert "nanovllm.engine.model_runner.build_planned_visual_embeddings" in done
+    import nanovllm.layers.attention as at
+    from nano_vllm_multimodal_b200.layers import attention as our_attention
+    assert at.flash_attn_with_kvcache is our_attention.flash_attn_with_kvcache
     tok = torch.zeros(3, 4)
     res = mr.build_planned_visual_embeddings(tok, SimpleNamespace(replacements=()), {})
     assert type(res) is mr.PlannedVisualEmbeddings and res.final_embedding is tok

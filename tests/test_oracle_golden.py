@@ -104,6 +104,21 @@ def test_deepstack(golden):
     _eq(O.add_deepstack_rows(i["hidden"], i["rows"], i["vis"]), c["outputs"]["y"])
 
 
+def test_decode_attention(golden):
+    """The float64 oracle against the reference's SDPA decode branch (CPU, bf16). That path
+    rounds intermediates in bf16, so the pin is a tolerance: |oracle - reference| <=
+    2^-6 * max(1, |reference|), and most elements agree exactly."""
+    c = golden["decode_attention_c2"]
+    i = c["inputs"]
+    o = O.paged_decode_attention(i["q"], i["k_cache"], i["v_cache"], i["context_lens"],
+                                 i["block_tables"], c["meta"]["scale"]).double()
+    ref = c["outputs"]["out"].double()
+    assert o.shape == ref.shape
+    assert bool(((o - ref).abs() <= 2.0 ** -6 * ref.abs().clamp(min=1.0)).all())
+    assert float((o == ref).double().mean()) > 0.6
+    assert torch.equal(o[0], ref[0])  # one-token context: softmax weight 1, exact
+
+
 def _visual_case(golden):
     c = golden["visual_merge_c3"]
     i = c["inputs"]
