@@ -193,6 +193,11 @@ __device__ __forceinline__ float sumsq_tree(const float* v) {
   return s[0];
 }
 
+// 1/sqrt(x) as the reference computes it in fp32: the correctly rounded square
+// root, then the correctly rounded reciprocal (IEEE sqrt.rn and rcp.rn, the
+// same two roundings as `1.0f / sqrtf(x)` without fast math).
+__device__ __forceinline__ float inv_sqrt_rn(float x) { return __frcp_rn(__fsqrt_rn(x)); }
+
 __device__ __forceinline__ void flag(unsigned int* status, unsigned int bit) {
   if (status != nullptr) atomicOr(status, bit);
 }

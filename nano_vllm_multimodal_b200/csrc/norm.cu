@@ -132,7 +132,7 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
       }
 #pragma unroll
       for (int off = G / 2; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-      const float rs = 1.0f / sqrtf(__fadd_rn(ss / static_cast<float>(n), eps));
+      const float rs = inv_sqrt_rn(__fadd_rn(ss / static_cast<float>(n), eps));
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int vi = i * G + gl;
@@ -217,7 +217,7 @@ rms_rows_block(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __r
     float tot = 0.f;
     for (int i = 0; i < nwarp; ++i) tot = __fadd_rn(tot, red[i]);
     __syncthreads();  // red is rewritten by the next row
-    const float rs = 1.0f / sqrtf(__fadd_rn(tot / static_cast<float>(n), eps));
+    const float rs = inv_sqrt_rn(__fadd_rn(tot / static_cast<float>(n), eps));
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = i * blockDim.x + threadIdx.x;

@@ -255,7 +255,7 @@ qk_prologue_pipe_kernel(const nib_qk_prologue_args a, const int stages, const ui
         }
 #pragma unroll
         for (int g = 0; g < kUG; ++g) {
-          const float rs = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss[g], 1.0f / D), a.eps));
+          const float rs = inv_sqrt_rn(__fadd_rn(__fmul_rn(ss[g], 1.0f / D), a.eps));
           const HeadWeights<T, W>& hw = isq[g] ? wq : wk;
           normalize_vec<T, W>(xa[g], wa[g], rs, hw.fa, hw.pa);
           normalize_vec<T, W>(xb[g], wb[g], rs, hw.fb, hw.pb);

@@ -173,7 +173,7 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
           float ss = __fadd_rn(sumsq_tree<E>(xa), sumsq_tree<E>(xb));
 #pragma unroll
           for (int off = L / 2; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-          const float rs = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / D), a.eps));
+          const float rs = inv_sqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / D), a.eps));
           const HeadWeights<T, W>& hw = is_q ? wq : wk;
           normalize_vec<T, W>(xa, wa, rs, hw.fa, hw.pa);
           normalize_vec<T, W>(xb, wb, rs, hw.fb, hw.pb);
