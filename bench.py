@@ -434,7 +434,7 @@ def cpu_baseline(budget_s: float, tokens: int = 2048) -> dict:
         cpu_layer(sample)
         reps += 1
         el = time.perf_counter() - t0
-        if el >= budget_s or reps >= 200:
+        if el >= budget_s:
             break
     return {"value": tokens * reps / el, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{reps} x one fused layer over {tokens} C5 tokens on the CPU oracle "
