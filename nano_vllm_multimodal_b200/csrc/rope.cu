@@ -82,15 +82,14 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
     const int chunk = static_cast<int>(it - t * nchunks);
     const int u0 = chunk * kChunk;
 
-    int64_t slot = -1;
-    if (store) {
-      const int32_t sv = __ldg(a.slot_mapping + t);
-      if (sv >= 0 && sv < a.num_slots) {
-        slot = sv;
-      } else if (sv != -1 && chunk == 0 && lane == 0) {
-        flag(a.status, NIB_DEV_BAD_SLOT);
-      }
-    }
+    // The slot and the 1-D table position are loaded together, and the v
+    // vectors are loaded whatever the slot, so that only the table row waits
+    // on a load (position -> row): two memory round trips per item, which is
+    // what bounds small decode batches.
+    const bool rotates = a.rope_mode != NIB_ROPE_NONE && u0 < Uq + Uk;
+    const int32_t sv = store ? __ldg(a.slot_mapping + t) : -1;
+    const int64_t tp = (rotates && a.rope_mode == NIB_ROPE_TABLE)
+                           ? __ldg(a.positions + t * a.positions_token_stride) : 0;
 
     // ---- issue every load of this item first (two vectors per lane per head)
     uint4 ba[kChunk], bb[kChunk];
@@ -105,7 +104,7 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
       } else if (u < Uq + Uk) {
         const int head = (u - Uq) * HPW + hs;
         if (head < nkv) src = k + t * a.k_token_stride + head * a.k_head_stride;
-      } else if (u < U && slot >= 0) {
+      } else if (u < U) {
         const int head = (u - Uq - Uk) * HPW + hs;
         if (head < nkv) src = v + t * a.v_token_stride + head * a.v_head_stride;
       }
@@ -115,13 +114,19 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
       }
     }
 
+    int64_t slot = -1;
+    if (sv >= 0 && sv < a.num_slots) {
+      slot = sv;
+    } else if (store && sv != -1 && chunk == 0 && lane == 0) {
+      flag(a.status, NIB_DEV_BAD_SLOT);
+    }
+
     // ---- cos / sin of this lane's E frequencies (only if the item rotates something)
     float c[E], s[E];
     uint32_t c2[4], s2[4];
-    const bool rotates = a.rope_mode != NIB_ROPE_NONE && u0 < Uq + Uk;
     if (rotates) {
       if (a.rope_mode == NIB_ROPE_TABLE) {
-        const int64_t p = __ldg(a.positions + t * a.positions_token_stride);
+        const int64_t p = tp;
         if (p >= 0 && p < a.table_rows) {
           const float* row = a.cos_sin_table + p * D;
 #pragma unroll
@@ -250,81 +255,134 @@ mrope_apply_kernel(const TX* __restrict__ x, int64_t xts, int64_t xhs, int64_t t
 }
 
 // Vectorised apply_multimodal_rotary_emb for head_dim 64/128/256 with cos/sin in
-// the activation dtype: a warp per token builds the selected cos/sin row of
-// the token in shared memory (the layout rule picks an axis per column), then
-// rotates its heads in the paired-halves layout, two 16-byte vectors per lane.
-// Same arithmetic as mrope_apply_kernel: chunked in fp32, interleaved in T
-// with every product and the sum rounded. Both halves read the selected value
-// of their own column (for interleaved the second half repeats column j).
+// the activation dtype, a warp per token. Paired-halves layout: lane l of a head
+// holds the E columns fb = l*E.. of the first half and their rotate-half
+// partners of the second half. Every load of the token is issued before any
+// math: the head vectors of up to kApplyGroups head groups, and one 16-byte
+// vector of each of the three axes' cos and sin rows at the lane's columns
+// (plus the second-half columns for the chunked strategy). The axis of each
+// column is fixed per lane, so selecting it is a register move, with no shared
+// memory. Same arithmetic as mrope_apply_kernel: chunked in fp32 with one
+// rounding, interleaved in T with every product and the sum rounded. The
+// second half reads column d for chunked and column j = d - D/2 for
+// interleaved (multimodal_rotary_embedding.py:33-45).
 constexpr int kApplyWarps = 4;
+constexpr int kApplyGroups = 4;  // head groups whose vectors are in flight together
 
-template <typename T, int D>
+template <typename T>
+__device__ __forceinline__ void select_axis(const uint4* v, uint32_t axes, float* f) {
+  constexpr int E = Elem<T>::kPerVec;
+  float a0[E], a1[E], a2[E];
+  unpack<T>(v[0], a0);
+  unpack<T>(v[1], a1);
+  unpack<T>(v[2], a2);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const uint32_t ax = (axes >> (2 * e)) & 3u;
+    f[e] = ax == 0 ? a0[e] : (ax == 1 ? a1[e] : a2[e]);
+  }
+}
+
+template <typename T, int D, bool INTER>
 __global__ void __launch_bounds__(kApplyWarps * 32)
 mrope_apply_vec_kernel(const T* __restrict__ x, int64_t xts, int64_t xhs, int64_t tokens, int heads,
                        const T* __restrict__ cos, const T* __restrict__ sin, int s0, int s1, int s2,
-                       int interleaved, T* __restrict__ out) {
+                       T* __restrict__ out) {
   constexpr int E = Elem<T>::kPerVec;
   constexpr int L = D / (2 * E);
   constexpr int HPW = 32 / L;
   constexpr int NF = D / 2;
-  __shared__ float sc[kApplyWarps][D], ss[kApplyWarps][D];
-  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  const int hs = lane / L, l = lane % L, fb = l * E;
+  constexpr bool inter = INTER;
+  const int lane = threadIdx.x & 31;
+  const int hs = lane / L, fb = (lane % L) * E;
   const int32_t sec[3] = {s0, s1, s2};
+  uint32_t axes = 0;  // 2 bits per column of this lane
+#pragma unroll
+  for (int e = 0; e < E; ++e) axes |= static_cast<uint32_t>(mrope_axis(fb + e, inter, sec)) << (2 * e);
+  const int groups = (heads + HPW - 1) / HPW;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   for (int64_t t = warp; t < tokens; t += nwarps) {
-    // the first head group's vectors are loaded before the cos/sin selection,
-    // and every group prefetches the next one's before its own math
-    uint4 na = zero_vec(), nb = zero_vec();
-    if (hs < heads) {
-      const T* src = x + t * xts + static_cast<int64_t>(hs) * xhs;
-      na = ld_stream(src + fb);
-      nb = ld_stream(src + NF + fb);
-    }
-    __syncwarp();
-    for (int d = lane; d < D; d += 32) {
-      const int j = d % NF;
-      const int axis = mrope_axis(j, interleaved != 0, sec);
-      const int col = interleaved ? j : d;
-      const int64_t o = (axis * tokens + t) * D + col;
-      sc[wib][d] = Elem<T>::to_f(cos[o]);
-      ss[wib][d] = Elem<T>::to_f(sin[o]);
-    }
-    __syncwarp();
-    float ca[E], cb[E], sa[E], sb[E];
+    const T* xt = x + t * xts;
+    uint4 va[kApplyGroups], vb[kApplyGroups];
+    auto load_heads = [&](int g0) {
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      ca[e] = sc[wib][fb + e];
-      cb[e] = sc[wib][NF + fb + e];
-      sa[e] = ss[wib][fb + e];
-      sb[e] = ss[wib][NF + fb + e];
-    }
-    for (int h0 = 0; h0 < heads; h0 += HPW) {
-      const int h = h0 + hs;
-      const uint4 va = na, vb = nb;
-      if (h + HPW < heads) {
-        const T* src = x + t * xts + static_cast<int64_t>(h + HPW) * xhs;
-        na = ld_stream(src + fb);
-        nb = ld_stream(src + NF + fb);
+      for (int g = 0; g < kApplyGroups; ++g) {
+        const int h = (g0 + g) * HPW + hs;
+        va[g] = vb[g] = zero_vec();
+        if (g0 + g < groups && h < heads) {
+          const T* src = xt + static_cast<int64_t>(h) * xhs;
+          va[g] = ld_stream(src + fb);
+          vb[g] = ld_stream(src + NF + fb);
+        }
       }
-      if (h >= heads) continue;
-      float xa[E], xb[E], ya[E], yb[E];
-      unpack<T>(va, xa);
-      unpack<T>(vb, xb);
+    };
+    uint4 cv[3], sv[3], cw[inter ? 1 : 3], sw[inter ? 1 : 3];
+#pragma unroll
+    for (int ax = 0; ax < 3; ++ax) {
+      const int64_t o = (ax * tokens + t) * D + fb;
+      cv[ax] = ld_stream(cos + o);
+      sv[ax] = ld_stream(sin + o);
+      if constexpr (!inter) {
+        cw[ax] = ld_stream(cos + o + NF);
+        sw[ax] = ld_stream(sin + o + NF);
+      }
+    }
+    load_heads(0);
+    float ca[E], sa[E], cb[E], sb[E];
+    select_axis<T>(cv, axes, ca);
+    select_axis<T>(sv, axes, sa);
+    if constexpr (inter) {
 #pragma unroll
       for (int e = 0; e < E; ++e) {
-        if (interleaved) {
-          ya[e] = round_to<T>(__fsub_rn(round_to<T>(__fmul_rn(xa[e], ca[e])), round_to<T>(__fmul_rn(xb[e], sa[e]))));
-          yb[e] = round_to<T>(__fadd_rn(round_to<T>(__fmul_rn(xb[e], cb[e])), round_to<T>(__fmul_rn(xa[e], sb[e]))));
-        } else {
+        cb[e] = ca[e];
+        sb[e] = sa[e];
+      }
+    } else {
+      select_axis<T>(cw, axes, cb);
+      select_axis<T>(sw, axes, sb);
+    }
+    uint32_t c2[4], s2[4];
+    pack_trig<T>(ca, sa, c2, s2);
+    T* ot = out + t * heads * static_cast<int64_t>(D);
+    for (int g0 = 0; g0 < groups; g0 += kApplyGroups) {
+      if (g0 > 0) load_heads(g0);
+#pragma unroll
+      for (int g = 0; g < kApplyGroups; ++g) {
+        const int h = (g0 + g) * HPW + hs;
+        if (g0 + g >= groups || h >= heads) continue;
+        uint32_t wa[4], wb[4];
+        from_u4(va[g], wa);
+        from_u4(vb[g], wb);
+        if constexpr (sizeof(T) == 2 && inter) {
+          {
+            using PK = Packed<T>;
+            using P = typename PK::P;
+#pragma unroll
+            for (int k = 0; k < E / 2; ++k) {
+              const P xa = pfrom<P>(wa[k]), xb = pfrom<P>(wb[k]);
+              const P cc = pfrom<P>(c2[k]), ss = pfrom<P>(s2[k]);
+              wa[k] = pbits(PK::sub(PK::mul(xa, cc), PK::mul(xb, ss)));
+              wb[k] = pbits(PK::add(PK::mul(xb, cc), PK::mul(xa, ss)));
+            }
+            T* dst = ot + static_cast<int64_t>(h) * D;
+            st_vec(dst + fb, as_u4(wa));
+            st_vec(dst + NF + fb, as_u4(wb));
+            continue;
+          }
+        }
+        float xa[E], xb[E], ya[E], yb[E];
+        unpack<T>(va[g], xa);
+        unpack<T>(vb[g], xb);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
           ya[e] = __fsub_rn(__fmul_rn(xa[e], ca[e]), __fmul_rn(xb[e], sa[e]));
           yb[e] = __fadd_rn(__fmul_rn(xb[e], cb[e]), __fmul_rn(xa[e], sb[e]));
         }
+        T* dst = ot + static_cast<int64_t>(h) * D;
+        st_vec(dst + fb, pack<T>(ya));
+        st_vec(dst + NF + fb, pack<T>(yb));
       }
-      T* dst = out + (t * heads + h) * D;
-      st_vec(dst + fb, pack<T>(ya));
-      st_vec(dst + NF + fb, pack<T>(yb));
     }
   }
 }
@@ -490,7 +548,8 @@ extern "C" int nib_mrope_apply(int x_dtype, const void* x, int64_t x_token_strid
   const int D = static_cast<int>(head_dim);
   const int E = 16 / elem_size(x_dtype);
   if (cos_dtype == x_dtype && (D == 64 || D == 128 || D == 256) && aligned16(x) && aligned16(out) &&
-      x_token_stride % E == 0 && x_head_stride % E == 0 && heads <= 65535) {
+      aligned16(cos) && aligned16(sin) && x_token_stride % E == 0 && x_head_stride % E == 0 &&
+      heads <= 65535) {
     // one-shot grid: 7% faster on B200 than 16 persistent CTAs per SM
     int64_t blocks = (tokens + kApplyWarps - 1) / kApplyWarps;
     const int64_t cap = kMaxGrid;
@@ -501,10 +560,12 @@ extern "C" int nib_mrope_apply(int x_dtype, const void* x, int64_t x_token_strid
     do {                                                                                           \
       auto run = [&](auto dtag) {                                                                  \
         constexpr int DD = decltype(dtag)::value;                                                  \
-        mrope_apply_vec_kernel<TT, DD><<<nb, th, 0, st>>>(                                         \
+        auto kern = interleaved ? mrope_apply_vec_kernel<TT, DD, true>                             \
+                                : mrope_apply_vec_kernel<TT, DD, false>;                           \
+        kern<<<nb, th, 0, st>>>(                                                                   \
             static_cast<const TT*>(x), x_token_stride, x_head_stride, tokens, static_cast<int>(heads), \
             static_cast<const TT*>(cos), static_cast<const TT*>(sin), sections[0], sections[1],   \
-            sections[2], interleaved, static_cast<TT*>(out));                                     \
+            sections[2], static_cast<TT*>(out));                                                  \
       };                                                                                           \
       if (D == 64) run(std::integral_constant<int, 64>{});                                         \
       else if (D == 128) run(std::integral_constant<int, 128>{});                                  \

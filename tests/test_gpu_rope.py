@@ -161,6 +161,35 @@ def test_generic_apply_matches_oracle(strategy, dtype):
         assert_bitexact(ak, ek, f"k {D} {dtype}")
 
 
+@pytest.mark.parametrize("strategy", ["chunked", "interleaved"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_vector_apply_head_counts_strides_alignment(strategy, dtype):
+    """The vectorised apply kernel over head counts that leave partial head groups
+    and several load chunks (1..40 heads), head dims 64/128/256, a strided view of
+    a wider row, and cos/sin whose base is not 16-byte aligned (the kernel must
+    then take the per-element path): bit-exact against the oracle every time."""
+    g = torch.Generator().manual_seed(31)
+    T = 37
+    for D, sections in ((64, (12, 10, 10)), (128, (24, 20, 20)), (256, (48, 40, 40))):
+        for heads in (1, 3, 16, 20, 40):
+            wide = torch.randn(T, heads + 3, D, generator=g).to(dtype)
+            x = wide[:, 2:2 + heads]
+            cos = torch.randn(3, T, D, generator=g).to(dtype)
+            sin = torch.randn(3, T, D, generator=g).to(dtype)
+            ex, _ = O.apply_mrope(x.contiguous(), x[:, :1].contiguous(), cos, sin, sections, strategy)
+            got = ops.mrope_apply(x.cuda(), cos.cuda(), sin.cuda(), sections, strategy == "interleaved")
+            assert_bitexact(got, ex, f"D={D} heads={heads} {dtype}")
+            if heads == 3:
+                n = cos.numel()
+                cbuf = torch.empty(2 * n + 1, dtype=dtype, device="cuda")
+                cm = cbuf[1:1 + n].view(3, T, D)
+                sm = cbuf[1 + n:].view(3, T, D)
+                cm.copy_(cos.cuda())
+                sm.copy_(sin.cuda())
+                got = ops.mrope_apply(x.cuda(), cm, sm, sections, strategy == "interleaved")
+                assert_bitexact(got, ex, f"misaligned cos/sin D={D} {dtype}")
+
+
 @pytest.mark.parametrize("D", [64, 128, 256, 12, 6, 2])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_mrope_cos_sin_head_dims_and_dtypes(D, dtype):
