@@ -237,8 +237,14 @@ template <typename T, typename W, int G, int VPT, int RB = 1, bool DS = false>
 static void launch_warp(const void* x, int64_t x_ts, int64_t x_hs, const void* res, int64_t r_rs,
                         const void* w, void* y, void* res_out, int64_t rows, int64_t heads, int n,
                         float eps, int add, int round_sum, cudaStream_t st, const DsArgs& ds) {
-  constexpr int kThreads = 256;
-  constexpr int rows_per_block = (kThreads / 32) * (32 / G) * RB;
+  int threads = 256;
+  // Few full-warp rows (decode batches): narrower CTAs so that the rows spread
+  // over every SM instead of queueing 8 to an SM on a few of them.
+  if (G == 32) {
+    const int64_t per_sm = (rows + sm_count() - 1) / sm_count();
+    if (per_sm < 8) threads = 32 * static_cast<int>(per_sm < 1 ? 1 : per_sm);
+  }
+  const int64_t rows_per_block = (threads / 32) * (32 / G) * RB;
   int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
   // Full-warp rows: one-shot CTAs (a retiring CTA's store drain overlaps the
   // next CTA's loads; measured 3% faster on B200 than 32 persistent CTAs per
@@ -246,7 +252,7 @@ static void launch_warp(const void* x, int64_t x_ts, int64_t x_hs, const void* r
   const int64_t cap = G < 32 ? static_cast<int64_t>(sm_count()) * 32 : kMaxGrid;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  rms_rows_warp<T, W, G, VPT, RB, DS><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+  rms_rows_warp<T, W, G, VPT, RB, DS><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
       static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
       static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
       add, round_sum, ds);
