@@ -688,8 +688,10 @@ def component_bench(inp, device, hbm_peak):
     qq = q[:32768]
     cos, sin = ops.mrope_cos_sin(pos, inp["inv_freq"], torch.bfloat16)
     ms = _time_op(flush=flush, fn=lambda: ops.mrope_apply(qq, cos, sin, SECTIONS, True))
-    record("mrope_apply_generic", ms, 32768 * NQ * D * 2 * 2 + 2 * 3 * 32768 * D * 2,
-           "C3 shapes, 32,768 tokens x 16 heads, cos/sin given")
+    # interleaved: both halves of a head read column j < D/2, so the op needs the
+    # first half of each axis row of cos and sin (every 32-byte sector of it)
+    record("mrope_apply_generic", ms, 32768 * NQ * D * 2 * 2 + 2 * 3 * 32768 * (D // 2) * 2,
+           "C3 shapes, 32,768 tokens x 16 heads, cos/sin given (first half of each axis row read)")
     ms = _time_op(flush=flush, fn=lambda: ops.mrope_cos_sin(pos, inp["inv_freq"], torch.bfloat16))
     record("mrope_cos_sin", ms, 3 * 32768 * 8 + 2 * 3 * 32768 * D * 2,
            "32,768 tokens, 3 axes (sincosf-bound: 6.3 M sincos per call)")
