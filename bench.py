@@ -74,7 +74,7 @@ def parse_args(argv=None):
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-components", action="store_true", help="skip the per-kernel extras")
-    p.add_argument("--component", choices=("decode_attention", "step_inputs"), default=None,
+    p.add_argument("--component", choices=("decode_attention", "step_inputs", "mrope"), default=None,
                    help="run only this standalone component (one GPU) and print its JSON")
     p.add_argument("--decode-requests", type=int, default=256,
                    help="requests of the decode-attention component (C2: 256)")
@@ -622,6 +622,24 @@ def decode_attention_component(out, record, flush, device, requests=256):
     del kc, vc
 
 
+def mrope_component(record, flush, q, positions, inv_freq):
+    """MultimodalRotaryEmbedding.cos_sin and apply_multimodal_rotary_emb on their
+    own (the model path computes cos/sin inside the fused prologue): C3 shapes,
+    32,768 tokens x 16 heads, q a strided view of the qkv rows."""
+    from nano_vllm_multimodal_b200 import ops
+
+    n = q.shape[0]
+    cos, sin = ops.mrope_cos_sin(positions, inv_freq, torch.bfloat16)
+    ms = _time_op(flush=flush, fn=lambda: ops.mrope_apply(q, cos, sin, SECTIONS, True))
+    # interleaved: both halves of a head read column j < D/2, so the op needs the
+    # first half of each axis row of cos and sin (every 32-byte sector of it)
+    record("mrope_apply_generic", ms, n * NQ * D * 2 * 2 + 2 * 3 * n * (D // 2) * 2,
+           f"C3 shapes, {n:,} tokens x 16 heads, cos/sin given (first half of each axis row read)")
+    ms = _time_op(flush=flush, fn=lambda: ops.mrope_cos_sin(positions, inv_freq, torch.bfloat16))
+    record("mrope_cos_sin", ms, 3 * n * 8 + 2 * 3 * n * D * 2,
+           f"{n:,} tokens, 3 axes (sincosf-bound: {3 * n * D // 2 / 1e6:.1f} M sincos per call)")
+
+
 def component_bench(inp, device, hbm_peak):
     """The path's kernels that the fused layer does not exercise on their own,
     each at a full config size, timed with CUDA events (working sets > L2)."""
@@ -683,18 +701,7 @@ def component_bench(inp, device, hbm_peak):
     visual_merge_component(out, record, flush, seeds, rows, c3)
     step_inputs_component(out, device)
     decode_attention_component(out, record, flush, device)
-    # generic M-RoPE apply on materialised cos/sin (apply_multimodal_rotary_emb)
-    pos = inp["positions"][:, :32768]
-    qq = q[:32768]
-    cos, sin = ops.mrope_cos_sin(pos, inp["inv_freq"], torch.bfloat16)
-    ms = _time_op(flush=flush, fn=lambda: ops.mrope_apply(qq, cos, sin, SECTIONS, True))
-    # interleaved: both halves of a head read column j < D/2, so the op needs the
-    # first half of each axis row of cos and sin (every 32-byte sector of it)
-    record("mrope_apply_generic", ms, 32768 * NQ * D * 2 * 2 + 2 * 3 * 32768 * (D // 2) * 2,
-           "C3 shapes, 32,768 tokens x 16 heads, cos/sin given (first half of each axis row read)")
-    ms = _time_op(flush=flush, fn=lambda: ops.mrope_cos_sin(pos, inp["inv_freq"], torch.bfloat16))
-    record("mrope_cos_sin", ms, 3 * 32768 * 8 + 2 * 3 * 32768 * D * 2,
-           "32,768 tokens, 3 axes (sincosf-bound: 6.3 M sincos per call)")
+    mrope_component(record, flush, q[:32768], inp["positions"][:, :32768], inp["inv_freq"])
     del flush
     out["c2_decode_layer_graph"] = decode_layer_graph(device)
     return out
@@ -933,6 +940,14 @@ def component_only(name, decode_requests=256):
 
     if name == "decode_attention":
         decode_attention_component(out, record, flush, device, decode_requests)
+    elif name == "mrope":
+        g = torch.Generator(device=device)
+        g.manual_seed(5300)
+        T = 32768
+        qkv = torch.randn(T, (NQ + 2 * NKV) * D, generator=g, device=device).to(torch.bfloat16)
+        pos = torch.randint(0, 32768, (3, T), generator=g, device=device)
+        inv = (1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).to(device)
+        mrope_component(record, flush, qkv[:, :NQ * D].view(T, NQ, D), pos, inv)
     else:
         step_inputs_component(out, device)
     print(json.dumps({"component": name, "peak_gbs": hbm_peak, **out}))

@@ -284,7 +284,7 @@ __device__ __forceinline__ void select_axis(const uint4* v, uint32_t axes, float
 }
 
 template <typename T, int D, bool INTER>
-__global__ void __launch_bounds__(kApplyWarps * 32)
+__global__ void __launch_bounds__(kApplyWarps * 32, INTER ? 6 : 4)
 mrope_apply_vec_kernel(const T* __restrict__ x, int64_t xts, int64_t xhs, int64_t tokens, int heads,
                        const T* __restrict__ cos, const T* __restrict__ sin, int s0, int s1, int s2,
                        T* __restrict__ out) {
@@ -321,11 +321,11 @@ mrope_apply_vec_kernel(const T* __restrict__ x, int64_t xts, int64_t xhs, int64_
 #pragma unroll
     for (int ax = 0; ax < 3; ++ax) {
       const int64_t o = (ax * tokens + t) * D + fb;
-      cv[ax] = ld_stream(cos + o);
-      sv[ax] = ld_stream(sin + o);
+      cv[ax] = ld_vec(cos + o);
+      sv[ax] = ld_vec(sin + o);
       if constexpr (!inter) {
-        cw[ax] = ld_stream(cos + o + NF);
-        sw[ax] = ld_stream(sin + o + NF);
+        cw[ax] = ld_vec(cos + o + NF);
+        sw[ax] = ld_vec(sin + o + NF);
       }
     }
     load_heads(0);
