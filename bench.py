@@ -74,7 +74,7 @@ def parse_args(argv=None):
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-components", action="store_true", help="skip the per-kernel extras")
-    p.add_argument("--component", choices=("decode_attention", "step_inputs", "mrope"), default=None,
+    p.add_argument("--component", choices=("decode_attention", "step_inputs", "mrope", "rows"), default=None,
                    help="run only this standalone component (one GPU) and print its JSON")
     p.add_argument("--decode-requests", type=int, default=256,
                    help="requests of the decode-attention component (C2: 256)")
@@ -458,6 +458,41 @@ def config_block(args, world, extra=None):
 # ------------------------------------------------------------------ other kernels of the path
 
 
+def _time_graph(calls, reps=24):
+    """Average ms per call of ``reps`` calls captured back to back in one CUDA
+    graph, cycling through ``calls``. Each callable owns a separate set of
+    inputs, and the sets together are several times the 126 MB L2, so no call
+    finds its inputs left in L2 by the call before; the outputs of all ``reps``
+    calls stay alive, so none writes into a buffer an earlier call left in L2.
+    The graph removes the host launch gaps of short kernels; each kernel starts
+    with the L2 that its predecessor left, as inside a model step."""
+    keep = []
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for c in calls:
+            keep.append(c())
+    torch.cuda.current_stream().wait_stream(side)
+    keep.clear()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(reps):
+            keep.append(calls[i % len(calls)]())
+    graph.replay()
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(3):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        graph.replay()
+        e.record()
+        e.synchronize()
+        ms = s.elapsed_time(e) / reps
+        best = ms if best is None else min(best, ms)
+    del graph, keep
+    return best
+
+
 def _time_op(fn, reps=20, warmup=3, flush=None):
     """Average ms of ``fn`` with CUDA events around each call; ``flush`` (a
     buffer larger than L2) is overwritten between calls, outside the events."""
@@ -622,20 +657,109 @@ def decode_attention_component(out, record, flush, device, requests=256):
     del kc, vc
 
 
-def mrope_component(record, flush, q, positions, inv_freq):
+def rows_flushed_rounds(flush, device, rounds=3):
+    """The row kernels one call at a time, each after an L2 flush, in rounds of
+    (embedding, DeepStack add, add + norm + DeepStack): the launch order a
+    profiler capture of `--component rows` relies on. Returns ms per call of
+    rounds 2.. (CUDA events around each call)."""
+    from nano_vllm_multimodal_b200 import ops, workloads as W
+
+    seeds = W._Seeds(2, device)
+    seeds.index = 800
+    emb = W._normal(seeds, (151936, 1024), 0.0, 0.02)
+    ids = torch.randint(0, 151936, (65536,), generator=seeds(), device=device)
+    c3 = W.C3
+    hs = W._normal(seeds, (c3.tokens, c3.hidden))
+    res = W._normal(seeds, (c3.tokens, c3.hidden))
+    wn = W._normal(seeds, (c3.hidden,), 1.0, 0.1)
+    vrows = W.deepstack_rows(3, c3.tokens).to(device)
+    vis = W._normal(seeds, (vrows.numel(), c3.hidden))
+    ridx = ops.deepstack_row_index(vrows, c3.tokens)
+    fns = {"embedding": lambda: ops.embedding(ids, emb),
+           "deepstack_add_inplace": lambda: ops.deepstack_add_(hs, vrows, vis),
+           "add_norm_deepstack": lambda: ops.add_rms_norm_deepstack(hs, res, wn, EPS, vis, ridx)}
+    ms = dict.fromkeys(fns, 0.0)
+    for r in range(rounds):
+        for name, fn in fns.items():
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            if r > 0:
+                ms[name] += s.elapsed_time(e) / (rounds - 1)
+    return ms
+
+
+SETS = 4  # separate input/output sets of a graph-timed component (together several times L2)
+
+
+def rows_component(record, seeds, device, out=None):
+    """The row kernels on their own, graph-timed over SETS input sets: the C2
+    embedding (65,536 random ids into the 151,936 x 1,024 table), the C3
+    DeepStack add in place and out of place, and the C3 add + norm + DeepStack
+    fold (32,768 tokens, 16,384 visual rows) next to the three passes it
+    replaces."""
+    from nano_vllm_multimodal_b200 import ops, workloads as W
+
+    embs = [W._normal(seeds, (151936, 1024), 0.0, 0.02) for _ in range(SETS)]
+    idss = [torch.randint(0, 151936, (65536,), generator=seeds(), device=device) for _ in range(SETS)]
+    ms = _time_graph([lambda i=i: ops.embedding(idss[i], embs[i]) for i in range(SETS)])
+    record("embedding", ms, 65536 * (4 * 1024 + 8), "C2 table 151936x1024, 65,536 random ids")
+    del embs, idss
+    c3 = W.C3
+    rows = W.deepstack_rows(3, c3.tokens).to(device)
+    hss = [W._normal(seeds, (c3.tokens, c3.hidden)) for _ in range(SETS)]
+    viss = [W._normal(seeds, (rows.numel(), c3.hidden)) for _ in range(SETS)]
+    ms = _time_graph([lambda i=i: ops.deepstack_add_(hss[i], rows, viss[i]) for i in range(SETS)])
+    record("deepstack_add_inplace", ms, rows.numel() * (6 * c3.hidden + 8),
+           "C3: hidden [32768,2048], 16,384 image rows")
+    ms = _time_graph([lambda i=i: ops.deepstack_add(hss[i], rows, viss[i]) for i in range(SETS)])
+    record("deepstack_add_out_of_place", ms, c3.tokens * 4 * c3.hidden + rows.numel() * (6 * c3.hidden + 8),
+           "C3, copy + add")
+    # Qwen3-VL layer boundary with DeepStack folded in: rounded add + visual-row add + text norm
+    ress = [W._normal(seeds, (c3.tokens, c3.hidden)) for _ in range(SETS)]
+    wn = W._normal(seeds, (c3.hidden,), 1.0, 0.1)
+    ridx = ops.deepstack_row_index(rows, c3.tokens)
+    ms = _time_graph([lambda i=i: ops.add_rms_norm_deepstack(hss[i], ress[i], wn, EPS, viss[i], ridx)
+                      for i in range(SETS)])
+
+    def unfused(i):
+        s = hss[i] + ress[i]
+        ops.deepstack_add_(s, rows, viss[i])
+        return ops.rms_norm(s, wn, EPS), s
+
+    ms_unfused = _time_graph([lambda i=i: unfused(i) for i in range(SETS)])
+    record("add_norm_deepstack", ms, c3.tokens * (8 * c3.hidden + 4) + rows.numel() * 2 * c3.hidden,
+           "C3: [32768,2048] + 16,384 visual rows, one pass")
+    if out is not None:
+        out["add_norm_deepstack"]["unfused_ms"] = round(ms_unfused, 4)
+        out["add_norm_deepstack"]["unfused"] = "torch add + deepstack_add_ + rms_norm"
+
+
+def mrope_component(record, device, inv_freq, tokens=32768):
     """MultimodalRotaryEmbedding.cos_sin and apply_multimodal_rotary_emb on their
-    own (the model path computes cos/sin inside the fused prologue): C3 shapes,
-    32,768 tokens x 16 heads, q a strided view of the qkv rows."""
+    own (the model path computes cos/sin inside the fused prologue), graph-timed
+    over SETS input sets: C3 shapes, 32,768 tokens x 16 heads, q a strided view
+    of the qkv rows, positions uniform on [0, 32767]."""
     from nano_vllm_multimodal_b200 import ops
 
-    n = q.shape[0]
-    cos, sin = ops.mrope_cos_sin(positions, inv_freq, torch.bfloat16)
-    ms = _time_op(flush=flush, fn=lambda: ops.mrope_apply(q, cos, sin, SECTIONS, True))
+    g = torch.Generator(device=device)
+    g.manual_seed(5300)
+    n = tokens
+    qkvs = [torch.randn(n, (NQ + 2 * NKV) * D, generator=g, device=device).to(torch.bfloat16)
+            for _ in range(SETS)]
+    qs = [t[:, :NQ * D].view(n, NQ, D) for t in qkvs]
+    poss = [torch.randint(0, 32768, (3, n), generator=g, device=device) for _ in range(SETS)]
+    trig = [ops.mrope_cos_sin(p, inv_freq, torch.bfloat16) for p in poss]
+    ms = _time_graph([lambda i=i: ops.mrope_apply(qs[i], trig[i][0], trig[i][1], SECTIONS, True)
+                      for i in range(SETS)])
     # interleaved: both halves of a head read column j < D/2, so the op needs the
     # first half of each axis row of cos and sin (every 32-byte sector of it)
     record("mrope_apply_generic", ms, n * NQ * D * 2 * 2 + 2 * 3 * n * (D // 2) * 2,
            f"C3 shapes, {n:,} tokens x 16 heads, cos/sin given (first half of each axis row read)")
-    ms = _time_op(flush=flush, fn=lambda: ops.mrope_cos_sin(positions, inv_freq, torch.bfloat16))
+    ms = _time_graph([lambda i=i: ops.mrope_cos_sin(poss[i], inv_freq, torch.bfloat16) for i in range(SETS)])
     record("mrope_cos_sin", ms, 3 * n * 8 + 2 * 3 * n * D * 2,
            f"{n:,} tokens, 3 axes (sincosf-bound: {3 * n * D // 2 / 1e6:.1f} M sincos per call)")
 
@@ -662,46 +786,15 @@ def component_bench(inp, device, hbm_peak):
     record("paged_store", ms, T * 4 * NKV * D * 2, f"C5: {T} tokens, k/v strided views of the qkv rows")
     ms = _time_op(flush=flush, fn=lambda: ops.rms_norm(q, inp["q_weight"], EPS))
     record("rms_norm_heads", ms, T * NQ * D * 2 * 2, f"C3/C5 q-norm: [{T},{NQ},{D}] strided view")
-    # C2 embedding table (151936 x 1024 bf16), a large batch of random ids
     seeds = W._Seeds(2, device)
     seeds.index = 700
-    emb = W._normal(seeds, (151936, 1024), 0.0, 0.02)
-    ids = torch.randint(0, 151936, (65536,), generator=seeds(), device=device)
-    ms = _time_op(flush=flush, fn=lambda: ops.embedding(ids, emb))
-    record("embedding", ms, 65536 * (4 * 1024 + 8), "C2 table 151936x1024, 65,536 random ids")
-    del emb
-    # C3 DeepStack: 16 sequences x 2048 tokens, 1024 image rows each
+    rows_component(record, seeds, device, out)
     c3 = W.C3
-    hs = W._normal(seeds, (c3.tokens, c3.hidden))
     rows = W.deepstack_rows(3, c3.tokens).to(device)
-    vis = W._normal(seeds, (rows.numel(), c3.hidden))
-    ms = _time_op(flush=flush, fn=lambda: ops.deepstack_add_(hs, rows, vis))
-    record("deepstack_add_inplace", ms, rows.numel() * (6 * c3.hidden + 8),
-           "C3: hidden [32768,2048], 16,384 image rows")
-    ms = _time_op(flush=flush, fn=lambda: ops.deepstack_add(hs, rows, vis))
-    record("deepstack_add_out_of_place", ms, c3.tokens * 4 * c3.hidden + rows.numel() * (6 * c3.hidden + 8),
-           "C3, copy + add")
-    # Qwen3-VL layer boundary with DeepStack folded in: rounded add + visual-row add + text norm
-    res = W._normal(seeds, (c3.tokens, c3.hidden))
-    wn = W._normal(seeds, (c3.hidden,), 1.0, 0.1)
-    ridx = ops.deepstack_row_index(rows, c3.tokens)
-    ms = _time_op(flush=flush, fn=lambda: ops.add_rms_norm_deepstack(hs, res, wn, EPS, vis, ridx))
-
-    def unfused():
-        s = hs + res
-        ops.deepstack_add_(s, rows, vis)
-        return ops.rms_norm(s, wn, EPS)
-
-    ms_unfused = _time_op(flush=flush, fn=unfused)
-    record("add_norm_deepstack", ms, c3.tokens * (8 * c3.hidden + 4) + rows.numel() * 2 * c3.hidden,
-           "C3: [32768,2048] + 16,384 visual rows, one pass")
-    out["add_norm_deepstack"]["unfused_ms"] = round(ms_unfused, 4)
-    out["add_norm_deepstack"]["unfused"] = "torch add + deepstack_add_ + rms_norm"
-    del hs, vis, res
     visual_merge_component(out, record, flush, seeds, rows, c3)
     step_inputs_component(out, device)
     decode_attention_component(out, record, flush, device)
-    mrope_component(record, flush, q[:32768], inp["positions"][:, :32768], inp["inv_freq"])
+    mrope_component(record, device, inp["inv_freq"])
     del flush
     out["c2_decode_layer_graph"] = decode_layer_graph(device)
     return out
@@ -940,14 +1033,18 @@ def component_only(name, decode_requests=256):
 
     if name == "decode_attention":
         decode_attention_component(out, record, flush, device, decode_requests)
+    elif name == "rows":
+        from nano_vllm_multimodal_b200 import workloads as W
+
+        flushed = rows_flushed_rounds(flush, device)
+        seeds = W._Seeds(2, device)
+        seeds.index = 700
+        rows_component(record, seeds, device, out)
+        for k, v in flushed.items():
+            out[k]["flushed_call_ms"] = round(v, 4)
     elif name == "mrope":
-        g = torch.Generator(device=device)
-        g.manual_seed(5300)
-        T = 32768
-        qkv = torch.randn(T, (NQ + 2 * NKV) * D, generator=g, device=device).to(torch.bfloat16)
-        pos = torch.randint(0, 32768, (3, T), generator=g, device=device)
         inv = (1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).to(device)
-        mrope_component(record, flush, qkv[:, :NQ * D].view(T, NQ, D), pos, inv)
+        mrope_component(record, device, inv)
     else:
         step_inputs_component(out, device)
     print(json.dumps({"component": name, "peak_gbs": hbm_peak, **out}))
