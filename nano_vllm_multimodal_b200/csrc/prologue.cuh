@@ -13,10 +13,17 @@ namespace nib {
 // longer than one row's load takes, so a deeper ring does not help). At that
 // shape the time follows the bytes moved: skipping all of the arithmetic saves
 // 5%, and a 16-warp layout measured within +-3% of this one.
+// Launches of at most kPipeFewTokens tokens use 8 warps x 2 stages instead:
+// at 32,768 tokens (a rank's share of the 262,144-token step at 8 GPUs, where
+// the SMs run at their 1,965 MHz maximum) that took 0.1086 ms against 0.1173
+// ms for 12 x 2. At 262,144 tokens the order of the two depends on the box:
+// 8 x 2 was 4-7% faster at 1,870-1,950 MHz and 4% slower at ~1,700 MHz.
 template <typename W>
 constexpr int pipe_max_warps() { return sizeof(W) == 4 ? 8 : 12; }
 constexpr int pipe_max_warps(bool fp32_weights) { return fp32_weights ? 8 : 12; }
 constexpr int pipe_max_stages(bool fp32_weights) { return fp32_weights ? 3 : 2; }
+constexpr int kPipeFewTokenWarps = 8;
+constexpr int64_t kPipeFewTokens = 65536;
 constexpr uint32_t kPipeSmemBudget = 220 * 1024;  // dynamic shared memory per CTA
 constexpr int64_t kPipeMinTokens = 2048;          // below this the register kernel is used
 
