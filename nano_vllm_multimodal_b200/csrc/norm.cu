@@ -237,12 +237,15 @@ template <typename T, typename W, int G, int VPT, int RB = 1, bool DS = false>
 static void launch_warp(const void* x, int64_t x_ts, int64_t x_hs, const void* res, int64_t r_rs,
                         const void* w, void* y, void* res_out, int64_t rows, int64_t heads, int n,
                         float eps, int add, int round_sum, cudaStream_t st, const DsArgs& ds) {
-  int threads = 256;
-  // Few full-warp rows (decode batches): narrower CTAs so that the rows spread
-  // over every SM instead of queueing 8 to an SM on a few of them.
+  // Full-warp rows: 4-warp CTAs (graph-timed on B200 over separate input sets,
+  // Qwen3-VL add + norm at H = 2048: 82.6 us vs 85.0 us with 8-warp CTAs at
+  // 32,768 rows, 621.9 vs 625.2 us at 262,144). Few rows (decode batches):
+  // narrower still, so that the rows spread over every SM instead of queueing
+  // on a few of them.
+  int threads = G == 32 ? 128 : 256;
   if (G == 32) {
     const int64_t per_sm = (rows + sm_count() - 1) / sm_count();
-    if (per_sm < 8) threads = 32 * static_cast<int>(per_sm < 1 ? 1 : per_sm);
+    if (per_sm < 4) threads = 32 * static_cast<int>(per_sm < 1 ? 1 : per_sm);
   }
   const int64_t rows_per_block = (threads / 32) * (32 / G) * RB;
   int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
