@@ -44,7 +44,7 @@ __device__ __forceinline__ int64_t ds_row(const DsArgs& ds, int64_t t) {
   return j;
 }
 
-template <typename T, typename W, int G, int VPT, int RB, bool DS = false>
+template <typename T, typename W, int G, int VPT, int RB, bool DS = false, bool PW = false>
 __global__ void __launch_bounds__(256)
 rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __restrict__ res,
               int64_t r_rs, const W* __restrict__ w, T* __restrict__ y, T* __restrict__ res_out,
@@ -60,10 +60,13 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int nv = n / E;
   const bool use_add = G == 32 && add != 0;  // short rows (G < 32) never carry a residual
-  // short rows: a lane's weight vectors are the same for every row - load once
+  // A lane's weight vectors are the same for every row: short rows load them
+  // once; full-warp rows do too when PW (small batches, where a weight load
+  // after the row's reduction would add a memory round trip to every warp).
+  constexpr bool kPreW = G < 32 || PW;
   float wfs[VPT][E];
   uint32_t wps[VPT][4];
-  if constexpr (G < 32) {
+  if constexpr (kPreW) {
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = i * G + gl;
@@ -139,7 +142,7 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
         if (!(active[b] && vi < nv)) continue;
         if (use_add) st_vec(res_out + r[b] * n + vi * E, pack<T>(v[i]));
         uint32_t words[4];
-        if constexpr (G < 32) {
+        if constexpr (kPreW) {
           normalize_vec<T, W>(v[i], words, rs, wfs[i], wps[i]);
         } else {
           float wf[E];
@@ -255,6 +258,14 @@ static void launch_warp(const void* x, int64_t x_ts, int64_t x_hs, const void* r
   const int64_t cap = G < 32 ? static_cast<int64_t>(sm_count()) * 32 : kMaxGrid;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
+  // a single wave of full-warp rows (decode batches) preloads the weights
+  if (G == 32 && rows <= static_cast<int64_t>(sm_count()) * 4) {
+    rms_rows_warp<T, W, G, VPT, RB, DS, true><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+        static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
+        static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
+        add, round_sum, ds);
+    return;
+  }
   rms_rows_warp<T, W, G, VPT, RB, DS><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
       static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
       static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
