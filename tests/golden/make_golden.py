@@ -1,7 +1,7 @@
 """Generate the golden fixtures by running the reference's OWN modules on the CPU.
 
 Run in a container that has the NanoInfer source checkout (read-only) at
-``$NANOINFER_REF`` (default ``/root/reference``):
+``$NANOINFER_REF`` (the default is ``REF`` below):
 
     TORCHDYNAMO_DISABLE=1 python tests/golden/make_golden.py
 
