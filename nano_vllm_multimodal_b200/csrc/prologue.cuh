@@ -6,18 +6,17 @@
 namespace nib {
 
 // CTA shape of the pipelined kernel (one CTA per SM). With 16-bit norm
-// weights (or no norm) the kernel fits 168 registers, so 12 warps with a
+// weights (or no norm) the kernel takes about 155 registers, so 12 warps with a
 // 2-stage ring (one token in flight per warp) fit; float32 weights need more
-// registers and use 8 warps x 3 stages. On a power-capped B200, 12 x 2
-// measured 2% faster than 8 x 3 (a warp spends microseconds per token, far
-// longer than one row's load takes, so a deeper ring does not help). At that
-// shape the time follows the bytes moved: skipping all of the arithmetic saves
-// 5%, and a 16-warp layout measured within +-3% of this one.
-// Launches of at most kPipeFewTokens tokens use 8 warps x 2 stages instead:
-// at 32,768 tokens (a rank's share of the 262,144-token step at 8 GPUs, where
-// the SMs run at their 1,965 MHz maximum) that took 0.1086 ms against 0.1173
-// ms for 12 x 2. At 262,144 tokens the order of the two depends on the box:
-// 8 x 2 was 4-7% faster at 1,870-1,950 MHz and 4% slower at ~1,700 MHz.
+// registers and use 8 warps x 3 stages. A warp spends microseconds per token,
+// far longer than one row's load takes, so a deeper ring does not help; the
+// time follows the bytes moved (skipping all of the arithmetic saves 5%).
+// Which warp count wins depends on the clock a box holds: at 262,144 tokens
+// 12 x 2 was 4% faster than 8 x 2 near 1,700 MHz and 4-7% slower at 1,870-1,950
+// MHz; a 16-warp layout measured within +-3% of 12 x 2. Launches of at most
+// kPipeFewTokens tokens use 8 x 2: at 32,768 tokens (a rank's share of the
+// 262,144-token step at 8 GPUs, where the SMs run at their 1,965 MHz maximum)
+// that took 0.1086 ms against 0.1173 ms for 12 x 2.
 template <typename W>
 constexpr int pipe_max_warps() { return sizeof(W) == 4 ? 8 : 12; }
 constexpr int pipe_max_warps(bool fp32_weights) { return fp32_weights ? 8 : 12; }
