@@ -817,22 +817,33 @@ def component_bench(inp, device, hbm_peak):
     decode_attention_component(out, record, flush, device)
     mrope_component(record, device, inp["inv_freq"])
     del flush
-    out["c2_decode_layer_graph"] = decode_layer_graph(device)
+    out["c2_decode_layer_graph"] = decode_layer_graph(device, 2)
+    out["c3_decode_layer_graph"] = decode_layer_graph(device, 3)
     return out
 
 
-def decode_layer_graph(device, layers=28, replays=50):
-    """C2 decode step (Qwen3-0.6B shapes, 256 tokens, 10% padded slots): the
-    fused elementwise layer x28 captured once in a CUDA graph and replayed.
-    Small batches are launch-bound, not HBM-bound: reported as time per layer."""
+def decode_layer_graph(device, config=2, layers=28, replays=50):
+    """A decode step's fused elementwise layer x28 (256 tokens), captured once in
+    a CUDA graph and replayed: C2 (Qwen3-0.6B shapes, 1-D RoPE, 10% padded
+    slots) or, with ``config=3``, Qwen3-VL-2B shapes (rounded add + text norm,
+    interleaved M-RoPE computed in the kernel). Small batches are launch-bound,
+    not HBM-bound: reported as time per layer."""
     from nano_vllm_multimodal_b200 import ops, workloads as W
-
-    d = W.make_layer_inputs(2, device=device)
-    shp = d["shape"]
-    nq, nkv, hd = shp.num_heads, shp.num_kv_heads, shp.head_dim
+    from nano_vllm_multimodal_b200.layers.multimodal_rotary_embedding import MultimodalRotaryEmbedding
     from nano_vllm_multimodal_b200.layers.rotary_embedding import RotaryEmbedding
 
-    table = RotaryEmbedding(hd, hd, shp.max_position, shp.theta).to(device).cos_sin_cache
+    d = W.make_layer_inputs(config, tokens=256, device=device)
+    shp = d["shape"]
+    nq, nkv, hd = shp.num_heads, shp.num_kv_heads, shp.head_dim
+    if shp.rope == "table":
+        table = RotaryEmbedding(hd, hd, shp.max_position, shp.theta).to(device).cos_sin_cache
+        rope = dict(rope_mode=ops.ROPE_TABLE, cos_sin_cache=table)
+    else:
+        mod = MultimodalRotaryEmbedding(head_dim=hd, base=shp.theta, sections=shp.sections,
+                                        strategy=shp.rope).to(device)
+        mode = ops.ROPE_MROPE_INTERLEAVED if shp.rope == "interleaved" else ops.ROPE_MROPE_CHUNKED
+        rope = dict(rope_mode=mode, inv_freq=mod.inv_freq, sections=shp.sections)
+    rounded = shp.qk_norm == "text"  # Qwen3-VL adds the residual in the activation dtype
     qkv = d["qkv"]
     q, k, v = qkv.split([nq * hd, nkv * hd, nkv * hd], -1)
     q, k, v = q.view(-1, nq, hd), k.view(-1, nkv, hd), v.view(-1, nkv, hd)
@@ -840,11 +851,11 @@ def decode_layer_graph(device, layers=28, replays=50):
     def step():
         h, res = d["hidden"], d["residual"]
         for _ in range(layers):
-            _, h1 = ops.add_rms_norm(h, res, d["w_in"], 1e-6)
+            _, h1 = ops.add_rms_norm(h, res, d["w_in"], 1e-6, rounded)
             ops.qk_prologue(q, k, v=v, positions=d["positions"], q_weight=d["q_weight"], k_weight=d["k_weight"],
-                            eps=1e-6, rope_mode=ops.ROPE_TABLE, cos_sin_cache=table, key_cache=d["key_cache"],
-                            value_cache=d["value_cache"], slot_mapping=d["slot_mapping"])
-            _, h2 = ops.add_rms_norm(d["attn_out"], h1, d["w_post"], 1e-6)
+                            eps=1e-6, key_cache=d["key_cache"], value_cache=d["value_cache"],
+                            slot_mapping=d["slot_mapping"], **rope)
+            _, h2 = ops.add_rms_norm(d["attn_out"], h1, d["w_post"], 1e-6, rounded)
             ops.silu_and_mul(d["gate_up"])
             h, res = d["hidden"], h2
 
@@ -868,12 +879,17 @@ def decode_layer_graph(device, layers=28, replays=50):
     torch.cuda.synchronize()
     us_layer = e0.elapsed_time(e1) * 1000.0 / (replays * layers)
     del graph
+    axes = 1 if shp.rope == "table" else 3
+    cfg = ("C2 decode: 256 tokens, hidden 1024, 16/8 heads, 1-D RoPE (theta 1e6), 10% slots -1, I=3072"
+           if config == 2 else
+           "Qwen3-VL-2B decode (C3 shapes): 256 tokens, hidden 2048, 16/8 heads, text norm, interleaved "
+           "M-RoPE [24,20,20] theta 5e6, I=6144")
     return {"us_per_layer": round(us_layer, 2), "launches_per_layer": 4,
-            "tokens": shp.tokens, "layers_per_graph": layers,
-            "bytes_per_layer": shp.tokens * (2 * 8 * shp.hidden + 2 * ((nq + 2 * nkv) * hd + nq * hd + nkv * hd
-                                                                        + 2 * nkv * hd) + 12 + 6 * shp.intermediate),
-            "config": "C2 decode: 256 tokens, hidden 1024, 16/8 heads, 1-D RoPE (theta 1e6), 10% slots -1, "
-                      "I=3072; 28 layers per captured graph"}
+            "tokens": shp.tokens if config == 2 else 256, "layers_per_graph": layers,
+            "bytes_per_layer": 256 * (2 * 8 * shp.hidden + 2 * ((nq + 2 * nkv) * hd + nq * hd + nkv * hd
+                                                               + 2 * nkv * hd) + 8 * axes + 4
+                                      + 6 * shp.intermediate),
+            "config": cfg + "; 28 layers per captured graph"}
 
 
 # ------------------------------------------------------------------ arms
