@@ -95,6 +95,21 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
     const int32_t sv = store ? __ldg(a.slot_mapping + t) : -1;
     const int64_t tp = (rotates && a.rope_mode == NIB_ROPE_TABLE)
                            ? __ldg(a.positions + t * a.positions_token_stride) : 0;
+    // M-RoPE: the positions and inverse frequencies of this lane's frequencies
+    // (j = lane, lane + 32, ...) are loaded here too, so sincosf waits on one load
+    constexpr int FPL = (NF + 31) / 32;
+    float mp[FPL], mf[FPL];
+    const bool mrope = rotates && a.rope_mode != NIB_ROPE_TABLE;
+#pragma unroll
+    for (int m = 0; m < FPL; ++m) {
+      const int j = lane + 32 * m;
+      mp[m] = mf[m] = 0.f;
+      if (mrope && j < NF) {
+        const int axis = mrope_axis(j, inter, a.sections);
+        mp[m] = static_cast<float>(__ldg(a.positions + axis * a.positions_axis_stride + t * a.positions_token_stride));
+        mf[m] = __ldg(a.inv_freq + j);
+      }
+    }
 
     // ---- issue every load of this item first (two vectors per lane per head)
     uint4 ba[CH], bb[CH];
@@ -146,13 +161,15 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
         }
       } else {
         __syncwarp();
-        for (int j = lane; j < NF; j += 32) {
-          const int axis = mrope_axis(j, inter, a.sections);
-          const int64_t p = __ldg(a.positions + axis * a.positions_axis_stride + t * a.positions_token_stride);
-          float sn, cs;
-          sincosf(__fmul_rn(static_cast<float>(p), __ldg(a.inv_freq + j)), &sn, &cs);
-          s_cos[wib][j] = round_to<T>(cs);
-          s_sin[wib][j] = round_to<T>(sn);
+#pragma unroll
+        for (int m = 0; m < FPL; ++m) {
+          const int j = lane + 32 * m;
+          if (j < NF) {
+            float sn, cs;
+            sincosf(__fmul_rn(mp[m], mf[m]), &sn, &cs);
+            s_cos[wib][j] = round_to<T>(cs);
+            s_sin[wib][j] = round_to<T>(sn);
+          }
         }
         __syncwarp();
 #pragma unroll
