@@ -807,6 +807,29 @@ def component_bench(inp, device, hbm_peak):
     record("paged_store", ms, T * 4 * NKV * D * 2, f"C5: {T} tokens, k/v strided views of the qkv rows")
     ms = _time_op(flush=flush, fn=lambda: ops.rms_norm(q, inp["q_weight"], EPS))
     record("rms_norm_heads", ms, T * NQ * D * 2 * 2, f"C3/C5 q-norm: [{T},{NQ},{D}] strided view")
+    # The step's prologue writes K/V to a random permutation of slots (the worst
+    # case). A serving engine gives each sequence whole 256-slot blocks, so
+    # consecutive tokens fill consecutive slots of a randomly chosen block. Both
+    # placements on the same inputs, one launch at a time after an L2 flush.
+    nblk = inp["key_cache"].shape[0]
+    g = torch.Generator(device=device)
+    g.manual_seed(5400)
+    blocks = torch.randperm(nblk, generator=g, device=device)[: -(-T // 256)]
+    tok = torch.arange(T, device=device)
+    block_slots = (blocks[tok // 256] * 256 + tok % 256).to(torch.int32)
+
+    def prologue(slots):
+        return ops.qk_prologue(q, k, v=v, positions=inp["positions"], q_weight=inp["q_weight"],
+                               k_weight=inp["k_weight"], eps=EPS, rope_mode=ops.ROPE_MROPE_INTERLEAVED,
+                               inv_freq=inp["inv_freq"], sections=SECTIONS, key_cache=inp["key_cache"],
+                               value_cache=inp["value_cache"], slot_mapping=slots)
+
+    for name, slots, what in (("qk_prologue_random_slots", inp["slot_mapping"], "a random permutation of slots"),
+                              ("qk_prologue_block_slots", block_slots,
+                               "consecutive tokens in consecutive slots of random 256-slot blocks")):
+        ms = _time_op(flush=flush, fn=lambda slots=slots: prologue(slots))
+        record(name, ms, T * BYTES["qk_prologue"], f"C5: {T} tokens, K/V written to {what}")
+    del block_slots, tok
     seeds = W._Seeds(2, device)
     seeds.index = 700
     rows_component(record, seeds, device, out)
