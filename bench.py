@@ -759,6 +759,46 @@ def rows_component(record, seeds, device, out=None):
         out["add_norm_deepstack"]["unfused"] = "torch add + deepstack_add_ + rms_norm"
 
 
+def rope_forward_component(record, device):
+    """The rotary modules' own forward (the drop-in path when a model is not
+    edited to call the fused prologue: RotaryEmbedding.forward and
+    MultimodalRotaryEmbedding.forward, one kernel each), graph-timed over
+    separate input sets: 1-D RoPE and interleaved M-RoPE at 32,768 tokens with
+    16/8 heads, chunked M-RoPE at C4 (8,312 tokens, 16/2 heads). q and k are
+    strided views of the qkv rows; bytes = q and k in and out + positions."""
+    from nano_vllm_multimodal_b200.layers.multimodal_rotary_embedding import MultimodalRotaryEmbedding
+    from nano_vllm_multimodal_b200.layers.rotary_embedding import RotaryEmbedding
+
+    g = torch.Generator(device=device)
+    g.manual_seed(5500)
+
+    def sets(n, T, nq, nkv, axes, maxpos):
+        out = []
+        for _ in range(n):
+            qkv = torch.randn(T, (nq + 2 * nkv) * D, generator=g, device=device).to(torch.bfloat16)
+            shape = (T,) if axes == 1 else (3, T)
+            out.append((qkv[:, :nq * D].view(T, nq, D), qkv[:, nq * D:(nq + nkv) * D].view(T, nkv, D),
+                        torch.randint(0, maxpos, shape, generator=g, device=device)))
+        return out
+
+    cases = (
+        ("rope_forward", RotaryEmbedding(D, D, 40960, 1e6), SETS, 32768, 16, 8, 1, 40960,
+         "RotaryEmbedding (Qwen3, theta 1e6): 32,768 tokens, 16/8 heads"),
+        ("mrope_forward_interleaved",
+         MultimodalRotaryEmbedding(head_dim=D, base=THETA, sections=SECTIONS, strategy="interleaved"),
+         SETS, 32768, 16, 8, 3, 32768, "MultimodalRotaryEmbedding interleaved (Qwen3-VL): 32,768 tokens, 16/8 heads"),
+        ("mrope_forward_chunked",
+         MultimodalRotaryEmbedding(head_dim=D, base=1e6, sections=(16, 24, 24), strategy="chunked"),
+         8, 8312, 16, 2, 3, 16384, "MultimodalRotaryEmbedding chunked (Qwen2.5-VL, C4): 8,312 tokens, 16/2 heads"),
+    )
+    for name, mod, n, T, nq, nkv, axes, maxpos, cfg in cases:
+        mod = mod.to(device)
+        st = sets(n, T, nq, nkv, axes, maxpos)
+        ms = _time_graph([lambda i=i: mod(st[i][2], st[i][0], st[i][1]) for i in range(n)])
+        record(name, ms, T * ((nq + nkv) * D * 2 * 2 + 8 * axes), cfg + "; graph-timed")
+        del st
+
+
 def mrope_component(record, device, inv_freq, tokens=32768):
     """MultimodalRotaryEmbedding.cos_sin and apply_multimodal_rotary_emb on their
     own (the model path computes cos/sin inside the fused prologue), graph-timed
@@ -839,6 +879,7 @@ def component_bench(inp, device, hbm_peak):
     step_inputs_component(out, device)
     decode_attention_component(out, record, flush, device)
     mrope_component(record, device, inp["inv_freq"])
+    rope_forward_component(record, device)
     del flush
     out["c2_decode_layer_graph"] = decode_layer_graph(device, 2)
     out["c3_decode_layer_graph"] = decode_layer_graph(device, 3)
@@ -1105,6 +1146,7 @@ def component_only(name, decode_requests=256):
     elif name == "mrope":
         inv = (1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).to(device)
         mrope_component(record, device, inv)
+        rope_forward_component(record, device)
     else:
         step_inputs_component(out, device)
     print(json.dumps({"component": name, "peak_gbs": hbm_peak, **out}))

@@ -16,7 +16,8 @@ namespace nib {
 // MHz; a 16-warp layout measured within +-3% of 12 x 2. Launches of at most
 // kPipeFewTokens tokens use 8 x 2: at 32,768 tokens (a rank's share of the
 // 262,144-token step at 8 GPUs, where the SMs run at their 1,965 MHz maximum)
-// that took 0.1086 ms against 0.1173 ms for 12 x 2.
+// that took 0.1086 ms against 0.1173 ms for 12 x 2 (chunked M-RoPE, whose fp32
+// rotation needs the warps, keeps 12).
 template <typename W>
 constexpr int pipe_max_warps() { return sizeof(W) == 4 ? 8 : 12; }
 constexpr int pipe_max_warps(bool fp32_weights) { return fp32_weights ? 8 : 12; }
