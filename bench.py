@@ -253,7 +253,8 @@ class LaunchTimer:
         out = {}
         for name, pairs in self.pairs.items():
             ms = [s.elapsed_time(e) for s, e in pairs]
-            out[name] = {"launches": len(ms), "total_ms": sum(ms), "avg_ms": sum(ms) / len(ms)}
+            out[name] = {"launches": len(ms), "total_ms": sum(ms), "avg_ms": sum(ms) / len(ms),
+                         "p50_ms": statistics.median(ms)}
         return out
 
 
@@ -1038,6 +1039,7 @@ def ours_arm(args, rank, world, local):
         algo = BYTES[name] * units
         gbs = algo / (s["avg_ms"] / 1000.0) / 1e9
         per_kernel[name] = {"launches": s["launches"], "avg_ms": round(s["avg_ms"], 4),
+                            "p50_ms": round(s["p50_ms"], 4),
                             "share": None, "bytes_per_launch": algo, "achieved_gbs": round(gbs, 1),
                             "frac": round(gbs / hbm_peak, 4)}
     total_k = sum(s["total_ms"] for s in kernels.values())
