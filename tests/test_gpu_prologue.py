@@ -246,6 +246,35 @@ def test_pipelined_variant_bit_identical_to_register_variant(head_dim, heads, mo
                 assert_bitexact(b, a, f"{name} norm={norm} store={store}")
 
 
+@pytest.mark.parametrize("variant", [1, 2])
+def test_fused_fp32_norm_weights(variant):
+    """Qwen3 RMSNorm with float32 weights on bf16 activations (``x.to(dtype).mul_(weight)``
+    keeps the activation dtype: n = bf16(x * rs), y = bf16(n * w)), 1-D RoPE and the paged
+    store, through both kernels (the pipelined one then takes its 8-warp x 3-stage layout),
+    bit-exact against the oracle composition in the kernels' summation order."""
+    T = 3000
+    d = W.make_layer_inputs(1, tokens=T)
+    shp = d["shape"]
+    nq, nkv = shp.num_heads, shp.num_kv_heads
+    qw, kw = d["q_weight"].float(), d["k_weight"].float()
+    table = O.rope_cos_sin_cache(128, shp.max_position, shp.theta)
+    qkv = d["qkv"].cuda()
+    q, k, v = qkv.split([nq * 128, nkv * 128, nkv * 128], -1)
+    kc, vc = d["key_cache"].cuda(), d["value_cache"].cuda()
+    aq, ak = ops.qk_prologue(q.view(-1, nq, 128), k.view(-1, nkv, 128), v=v.view(-1, nkv, 128),
+                             positions=d["positions"].cuda(), q_weight=qw.cuda(), k_weight=kw.cuda(), eps=1e-6,
+                             rope_mode=ops.ROPE_TABLE, cos_sin_cache=table.cuda(), key_cache=kc, value_cache=vc,
+                             slot_mapping=d["slot_mapping"].cuda(), variant=variant)
+    eq, ek, ekc, evc = O.qk_norm_rope_store(
+        d["qkv"], nq, nkv, 128, positions=d["positions"], rope=("table", table), q_weight=qw, k_weight=kw,
+        eps=1e-6, norm="rms", key_cache=d["key_cache"], value_cache=d["value_cache"],
+        slot_mapping=d["slot_mapping"], order="kernel")
+    assert_bitexact(aq, eq, "q")
+    assert_bitexact(ak, ek, "k")
+    assert_bitexact(kc, ekc, "key cache")
+    assert_bitexact(vc, evc, "value cache")
+
+
 def test_pipelined_variant_rejects_split_layouts():
     T = 64
     q = torch.randn(T, 16, 128, dtype=torch.bfloat16, device="cuda")
