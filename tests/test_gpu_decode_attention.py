@@ -104,3 +104,46 @@ def test_bad_block_and_length_reported(monkeypatch):
     long[1] = 10_000
     with pytest.raises(ValueError, match="out of range"):
         ops.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), long.cuda(), tb.cuda(), 0.1)
+
+
+@pytest.mark.parametrize("batch", [4, 128])
+def test_drop_in_captures_in_a_cuda_graph(batch):
+    """ModelRunner captures its decode steps in CUDA graphs, attention included. The
+    drop-in reads no device value on the host, so it captures; replays with new
+    queries, context lengths and block tables written in place equal eager calls.
+    4 requests split their contexts over CTAs (partials in the workspace); 128 do not."""
+    nq, nkv, D, bs, width = 16, 8, 128, 256, 8
+    g = torch.Generator().manual_seed(batch)
+    nblocks = batch * width
+    kc = torch.randn(nblocks, bs, nkv, D, generator=g).to(torch.bfloat16).cuda()
+    vc = torch.randn(nblocks, bs, nkv, D, generator=g).to(torch.bfloat16).cuda()
+    q = torch.empty(batch, 1, nq, D, dtype=torch.bfloat16, device="cuda")
+    lens = torch.empty(batch, dtype=torch.int32, device="cuda")
+    tables = torch.empty(batch, width, dtype=torch.int32, device="cuda")
+
+    def fill(seed):
+        gg = torch.Generator().manual_seed(seed)
+        q.copy_(torch.randn(batch, 1, nq, D, generator=gg).to(torch.bfloat16))
+        lens.copy_(torch.randint(1, width * bs + 1, (batch,), generator=gg).to(torch.int32))
+        tables.copy_(torch.randperm(nblocks, generator=gg).view(batch, width).to(torch.int32))
+
+    def call():
+        return flash_attn_with_kvcache(q, kc, vc, cache_seqlens=lens, block_table=tables,
+                                       softmax_scale=D ** -0.5, causal=True)
+
+    fill(1)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        call()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = call()
+    for seed in (2, 3):
+        fill(seed)
+        graph.replay()
+        eager = call()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager), f"replay {seed}"
+    del graph
