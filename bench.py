@@ -596,7 +596,8 @@ def step_inputs_component(out, device):
     """Host -> device step inputs of a C3 prefill (32,768 tokens, 16 sequences, 3-axis
     positions): the reference's one pinned tensor + one copy per array
     (model_runner.py:700-725,823-870) vs one StepInputStager copy. Host wall time
-    per step (list conversion included), both from the same Python lists."""
+    per step (list conversion included), both from the same Python lists. Then the
+    same for a decode step's five arrays (model_runner.py:892-935)."""
     from nano_vllm_multimodal_b200.step_inputs import StepInputStager
 
     g = torch.Generator().manual_seed(4242)
@@ -632,6 +633,36 @@ def step_inputs_component(out, device):
         torch.cuda.synchronize()
     res.update(copies_reference=8, copies_staged=1, bytes_per_step=T * 8 * 4 + T * 4 + (B + 1) * 8 + B * 8 + B * 8 * 4,
                config="C3 prefill step inputs: 32,768 tokens, 16 sequences, 3-axis positions")
+
+    # decode (model_runner.py:892-935): 256 requests, contexts U[1, 8192], 3-axis positions
+    R = 256
+    dlens = torch.randint(1, 8193, (R,), generator=g).tolist()
+    dids = torch.randint(0, 151936, (R,), generator=g).tolist()
+    dpos = [[n - 1 for n in dlens]] * 3
+    dtables = [torch.randperm(8192, generator=g)[:(n + 255) // 256].tolist() for n in dlens]
+    dslots = [t[-1] * 256 + (n - 1) % 256 for t, n in zip(dtables, dlens)]
+
+    def decode_reference():
+        def cp(v, dt):
+            return torch.tensor(v, dtype=dt, pin_memory=True).cuda(non_blocking=True)
+        width = max(len(t) for t in dtables)
+        return (cp(dids, torch.int64), cp(dpos, torch.int64), cp(dslots, torch.int32), cp(dlens, torch.int32),
+                cp([t + [-1] * (width - len(t)) for t in dtables], torch.int32))
+
+    def decode_staged():
+        return stager.decode_inputs(dids, dpos, dslots, dlens, dtables, position_axes=3)
+
+    for name, fn in (("decode_reference_host_ms", decode_reference), ("decode_staged_host_ms", decode_staged)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(50):
+            fn()
+        res[name] = round((time.perf_counter() - t0) / 50 * 1e3, 4)
+        torch.cuda.synchronize()
+    res.update(decode_copies_reference=5, decode_copies_staged=1,
+               decode_config="C3 decode step inputs: 256 requests, contexts U[1, 8192], 3-axis positions")
     out["step_inputs"] = res
 
 

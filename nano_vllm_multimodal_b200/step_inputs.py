@@ -2,8 +2,10 @@
 
 The reference builds each per-step input array as its own pinned tensor and
 copies it with its own non-blocking ``.cuda()``
-(``nanovllm/engine/model_runner.py:700-725,823-870``: token ids, positions,
-cu_seqlens_q/k, slot mapping, context lengths, query starts, block tables).
+(``nanovllm/engine/model_runner.py:700-725,823-870`` for prefill: token ids,
+positions, cu_seqlens_q/k, slot mapping, context lengths, query starts, block
+tables; ``model_runner.py:892-935`` for decode: token ids, positions, slot
+mapping, context lengths, block tables).
 :class:`StepInputStager` converts the arrays once into contiguous host arrays,
 writes them into one slot of a small ring of pinned buffers and moves the slot
 with one ``cudaMemcpyAsync`` into one device allocation; the returned tensors
@@ -76,14 +78,36 @@ class StepInputStager:
                   (cu_seqlens_k, torch.int32), (slot_mapping, torch.int32), (full_context_lens, torch.int32),
                   (query_start_lens, torch.int32)]
         if block_tables is not None:
-            width = max((len(b) for b in block_tables), default=0)
-            padded = np.full((len(block_tables), width), -1, dtype=np.int32)
-            for i, b in enumerate(block_tables):
-                padded[i, :len(b)] = b
             names.append("block_tables")
-            arrays.append((padded, torch.int32))
+            arrays.append((_padded_tables(block_tables), torch.int32))
         out = dict(zip(names, self.stage(*arrays)))
         if position_axes == 1 and out["positions"].dim() == 2:
             out["positions"] = out["positions"][0]
         out.setdefault("block_tables", None)
         return out
+
+    def decode_inputs(self, input_ids, position_rows, slot_mapping, context_lens, block_tables,
+                      position_axes: int = 1):
+        """The tensors ``ModelRunner.prepare_decode`` creates (model_runner.py:892-935),
+        one token per sequence, staged together: a dict with ``input_ids`` (int64 [B]),
+        ``positions`` (int64 [B] when ``position_axes == 1`` else [axes, B]),
+        ``slot_mapping`` and ``context_lens`` (int32 [B]) and ``block_tables`` (int32
+        [B, max], rows padded with -1 as model_runner.py:696-707). The reference makes
+        five pinned tensors and five copies for these every decode step."""
+        names = ["input_ids", "positions", "slot_mapping", "context_lens", "block_tables"]
+        arrays = [(input_ids, torch.int64), (position_rows, torch.int64), (slot_mapping, torch.int32),
+                  (context_lens, torch.int32), (_padded_tables(block_tables), torch.int32)]
+        out = dict(zip(names, self.stage(*arrays)))
+        if position_axes == 1 and out["positions"].dim() == 2:
+            out["positions"] = out["positions"][0]
+        return out
+
+
+def _padded_tables(block_tables) -> np.ndarray:
+    """Block tables as one int32 [B, max] array, rows padded with -1
+    (model_runner.py:696-707)."""
+    width = max((len(b) for b in block_tables), default=0)
+    padded = np.full((len(block_tables), width), -1, dtype=np.int32)
+    for i, b in enumerate(block_tables):
+        padded[i, :len(b)] = b
+    return padded

@@ -80,3 +80,36 @@ def test_mixed_dtypes_and_empty_arrays():
     assert out[2].tolist() == list(range(5))
     assert out[3].shape == (2, 2) and int(out[3].sum()) == 4
     assert st.stage() == []
+
+
+@pytest.mark.parametrize("axes", [1, 3])
+def test_decode_inputs_match_the_reference_tensors(axes):
+    """prepare_decode's five tensors (model_runner.py:892-935): one token per
+    sequence, positions len - 1 (+ the M-RoPE delta on every axis), block tables
+    of different lengths padded with -1."""
+    g = torch.Generator().manual_seed(10 + axes)
+    B = 37
+    lens = torch.randint(1, 3000, (B,), generator=g).tolist()
+    ids = torch.randint(0, 151936, (B,), generator=g).tolist()
+    delta = torch.randint(-500, 500, (B,), generator=g).tolist() if axes == 3 else [0] * B
+    row = [n - 1 + d for n, d in zip(lens, delta)]
+    pos_rows = [row for _ in range(axes)]
+    tables = [torch.randperm(4096, generator=g)[:(n + 255) // 256].tolist() for n in lens]
+    slots = [t[-1] * 256 + (n - 1) % 256 for t, n in zip(tables, lens)]
+
+    def cp(v, dt):
+        return torch.tensor(v, dtype=dt, pin_memory=True).cuda(non_blocking=True)
+    width = max(len(t) for t in tables)
+    exp = dict(input_ids=cp(ids, torch.int64), positions=cp(pos_rows, torch.int64),
+               slot_mapping=cp(slots, torch.int32), context_lens=cp(lens, torch.int32),
+               block_tables=cp([t + [-1] * (width - len(t)) for t in tables], torch.int32))
+    if axes == 1:
+        exp["positions"] = exp["positions"][0]
+    st = StepInputStager(slots=2)
+    for _ in range(2):  # a second step reuses the ring
+        got = st.decode_inputs(ids, pos_rows, slots, lens, tables, position_axes=axes)
+        torch.cuda.synchronize()
+        assert set(got) == set(exp)
+        for name, t in exp.items():
+            assert got[name].dtype == t.dtype and got[name].shape == t.shape, name
+            assert torch.equal(got[name], t), name
