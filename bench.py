@@ -1020,6 +1020,10 @@ def reference_arm(args, rank, world):
 def ours_arm(args, rank, world, local):
     from nano_vllm_multimodal_b200 import ops  # noqa: F401  (loads the extension, fails loudly)
 
+    visible = torch.cuda.device_count()
+    if local >= visible:
+        raise SystemExit(f"bench.py: rank {rank} wants cuda:{local} but {visible} GPU(s) are visible; "
+                         f"run one rank per GPU (--nproc-per-node <= {visible})")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if world > 1:
