@@ -222,3 +222,16 @@ def test_visual_merge_reports_the_first_error_in_plan_order():
         build(tok, _vm_plan([(0, "a", 0), (1, "a", 7), (9, "a", 0)]), feats)
     with pytest.raises(IndexError, match="visual output row is out of range: -1"):
         build(tok, _vm_plan([(0, "a", 0), (-1, "a", 7)]), feats)  # output row is checked first
+
+
+def test_step_input_block_tables_are_padded_as_the_reference_pads_them():
+    """prepare_block_tables (model_runner.py:696-707): rows of different lengths,
+    padded on the right with -1 to the longest; an empty batch gives [0, 0]."""
+    from nano_vllm_multimodal_b200.step_inputs import _padded_tables, host_array
+
+    t = _padded_tables([[4, 5, 6], [7], [], [1, 2]])
+    assert t.dtype.name == "int32" and t.shape == (4, 3)
+    assert t.tolist() == [[4, 5, 6], [7, -1, -1], [-1, -1, -1], [1, 2, -1]]
+    assert _padded_tables([]).shape == (0, 0)
+    h = host_array(t, torch.int32)
+    assert h.dtype == torch.int32 and h.shape == (4, 3) and h.tolist() == t.tolist()
