@@ -27,12 +27,14 @@ _CODE = {torch.int64: "q", torch.int32: "i", torch.float32: "f"}  # array module
 
 
 def host_array(values, dtype: torch.dtype) -> torch.Tensor:
-    """A contiguous CPU tensor of `dtype` from a list (a list of equal-length
-    lists for 2-D), a numpy array or a tensor. Python lists go through the
-    ``array`` module, which converts ints about 1.6x faster than numpy."""
+    """A contiguous CPU tensor of `dtype` from a list or tuple (of equal-length
+    lists or tuples for 2-D, e.g. the decode position rows of
+    model_runner.py:326-337), a numpy array or a tensor. Python sequences go
+    through the ``array`` module, which converts ints about 1.6x faster than
+    numpy."""
     if isinstance(values, torch.Tensor):
         return values.to(dtype=dtype, device="cpu").contiguous()
-    if isinstance(values, list) and values:
+    if isinstance(values, (list, tuple)) and values:
         if isinstance(values[0], (list, tuple)):
             n = len(values[0])
             if n and all(len(r) == n for r in values):

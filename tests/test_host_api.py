@@ -9,6 +9,7 @@ import os
 from types import SimpleNamespace
 from unittest.mock import patch
 
+import numpy as np
 import pytest
 import torch
 
@@ -235,3 +236,7 @@ def test_step_input_block_tables_are_padded_as_the_reference_pads_them():
     assert _padded_tables([]).shape == (0, 0)
     h = host_array(t, torch.int32)
     assert h.dtype == torch.int32 and h.shape == (4, 3) and h.tolist() == t.tolist()
+    rows = tuple((5, 6, 7) for _ in range(3))  # build_decode_position_rows' tuple of tuples
+    for v in (rows, [list(r) for r in rows], rows[0], list(rows[0]), np.asarray(rows)):
+        h = host_array(v, torch.int64)
+        assert h.dtype == torch.int64 and h.tolist() == np.asarray(v).tolist()
