@@ -74,7 +74,8 @@ def parse_args(argv=None):
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-components", action="store_true", help="skip the per-kernel extras")
-    p.add_argument("--component", choices=("decode_attention", "step_inputs", "mrope", "rows"), default=None,
+    p.add_argument("--component", choices=("decode_attention", "step_inputs", "mrope", "rows", "visual_merge"),
+                   default=None,
                    help="run only this standalone component (one GPU) and print its JSON")
     p.add_argument("--decode-requests", type=int, default=256,
                    help="requests of the decode-attention component (C2: 256)")
@@ -1180,6 +1181,12 @@ def component_only(name, decode_requests=256):
         rows_component(record, seeds, device, out)
         for k, v in flushed.items():
             out[k]["flushed_call_ms"] = round(v, 4)
+    elif name == "visual_merge":
+        from nano_vllm_multimodal_b200 import workloads as W
+
+        seeds = W._Seeds(2, device)
+        seeds.index = 700
+        visual_merge_component(out, record, flush, seeds, W.deepstack_rows(3, W.C3.tokens).to(device), W.C3)
     elif name == "mrope":
         inv = (1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).to(device)
         mrope_component(record, device, inv)
