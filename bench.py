@@ -74,7 +74,8 @@ def parse_args(argv=None):
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-components", action="store_true", help="skip the per-kernel extras")
-    p.add_argument("--component", choices=("decode_attention", "step_inputs", "mrope", "rows", "visual_merge"),
+    p.add_argument("--component",
+                   choices=("decode_attention", "step_inputs", "mrope", "rows", "visual_merge", "paged_store"),
                    default=None,
                    help="run only this standalone component (one GPU) and print its JSON")
     p.add_argument("--decode-requests", type=int, default=256,
@@ -1187,6 +1188,20 @@ def component_only(name, decode_requests=256):
         seeds = W._Seeds(2, device)
         seeds.index = 700
         visual_merge_component(out, record, flush, seeds, W.deepstack_rows(3, W.C3.tokens).to(device), W.C3)
+    elif name == "paged_store":
+        # nanovllm_paged_kv::store alone at C5 head shapes: 65,536 tokens, k/v strided
+        # views of qkv rows, random slots of a 1,024-block cache pair (about 2 GB in all)
+        T = 65536
+        g = torch.Generator(device=device).manual_seed(91)
+        qkv = torch.randn(T, (NQ + 2 * NKV) * D, generator=g, device=device).to(torch.bfloat16)
+        k = qkv[:, NQ * D:(NQ + NKV) * D].view(-1, NKV, D)
+        v = qkv[:, (NQ + NKV) * D:].view(-1, NKV, D)
+        kc = torch.zeros(1024, 256, NKV, D, dtype=torch.bfloat16, device=device)
+        vc = torch.zeros_like(kc)
+        slots = torch.randperm(kc.shape[0] * 256, generator=g, device=device)[:T].to(torch.int32)
+        ms = _time_op(flush=flush, fn=lambda: ops.paged_store(k, v, kc, vc, slots))
+        record("paged_store", ms, T * 4 * NKV * D * 2, f"C5 heads: {T} tokens, k/v strided views of the qkv rows, "
+               "random slots; one call at a time after an L2 flush")
     elif name == "mrope":
         inv = (1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).to(device)
         mrope_component(record, device, inv)
