@@ -75,7 +75,8 @@ def parse_args(argv=None):
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-components", action="store_true", help="skip the per-kernel extras")
     p.add_argument("--component",
-                   choices=("decode_attention", "step_inputs", "mrope", "rows", "visual_merge", "paged_store"),
+                   choices=("decode_attention", "step_inputs", "mrope", "rows", "visual_merge", "paged_store",
+                            "head_norm"),
                    default=None,
                    help="run only this standalone component (one GPU) and print its JSON")
     p.add_argument("--decode-requests", type=int, default=256,
@@ -1202,6 +1203,17 @@ def component_only(name, decode_requests=256):
         ms = _time_op(flush=flush, fn=lambda: ops.paged_store(k, v, kc, vc, slots))
         record("paged_store", ms, T * 4 * NKV * D * 2, f"C5 heads: {T} tokens, k/v strided views of the qkv rows, "
                "random slots; one call at a time after an L2 flush")
+    elif name == "head_norm":
+        # Qwen3 q_norm alone (RMSNorm over each head of a strided q view of the qkv
+        # rows): 65,536 tokens x 16 heads of 128, bf16 weights
+        T = 65536
+        g = torch.Generator(device=device).manual_seed(92)
+        qkv = torch.randn(T, (NQ + 2 * NKV) * D, generator=g, device=device).to(torch.bfloat16)
+        q = qkv[:, : NQ * D].view(-1, NQ, D)
+        w = (1.0 + 0.1 * torch.randn(D, generator=g, device=device)).to(torch.bfloat16)
+        ms = _time_op(flush=flush, fn=lambda: ops.rms_norm(q, w, EPS))
+        record("rms_norm_heads", ms, T * NQ * D * 2 * 2, f"q-norm: [{T},{NQ},{D}] strided view of the qkv rows; "
+               "one call at a time after an L2 flush")
     elif name == "mrope":
         inv = (1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).to(device)
         mrope_component(record, device, inv)

@@ -17,7 +17,8 @@ def test_defaults_finish_within_the_contract():
     assert a.warmup >= 3
 
 
-@pytest.mark.parametrize("name", ["decode_attention", "step_inputs", "mrope", "rows", "visual_merge", "paged_store"])
+@pytest.mark.parametrize("name", ["decode_attention", "step_inputs", "mrope", "rows", "visual_merge", "paged_store",
+                                  "head_norm"])
 def test_every_standalone_component_is_accepted(name):
     assert bench.parse_args(["--component", name]).component == name
 
