@@ -45,7 +45,7 @@ __device__ __forceinline__ int64_t ds_row(const DsArgs& ds, int64_t t) {
 }
 
 template <typename T, typename W, int G, int VPT, int RB, bool DS = false, bool PW = false>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, G < 32 ? 2 : 1)
 rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __restrict__ res,
               int64_t r_rs, const W* __restrict__ w, T* __restrict__ y, T* __restrict__ res_out,
               int64_t rows, int64_t heads, int n, float eps, int add, int round_sum, DsArgs ds) {
@@ -80,14 +80,31 @@ rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __re
     uint4 xr[RB][VPT], rr[RB][VPT], dr[RB][DS ? VPT : 1];
     int64_t r[RB], dj[RB];
     bool active[RB];
+    // token and head of this lane's row in batch 0; batch b is b * GPW rows
+    // further on, so one division per step serves all RB batches
+    int64_t tt = 0, hh = 0;
+    if (heads != 1) {
+      tt = (rb + sub) / heads;
+      hh = rb + sub - tt * heads;
+    }
 #pragma unroll
     for (int b = 0; b < RB; ++b) {
       r[b] = rb + b * GPW + sub;
       active[b] = r[b] < rows;
+      if (heads != 1 && b > 0) {
+        hh += GPW;
+        if (heads >= GPW) {
+          if (hh >= heads) { hh -= heads; ++tt; }
+        } else {  // fewer heads than rows per batch: several tokens on
+          const int q = static_cast<int>(hh) / static_cast<int>(heads);
+          tt += q;
+          hh -= static_cast<int64_t>(q) * heads;
+        }
+      }
       int64_t t = 0, h = 0;
       if (active[b]) {
-        t = heads == 1 ? r[b] : r[b] / heads;
-        h = r[b] - t * heads;
+        t = heads == 1 ? r[b] : tt;
+        h = heads == 1 ? 0 : hh;
       }
       if constexpr (DS) dj[b] = active[b] ? ds_row(ds, t) : -1;  // heads == 1
       const T* xp = x + t * x_ts + h * x_hs;
