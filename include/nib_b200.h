@@ -311,7 +311,10 @@ NIB_API int nib_paged_gather_varlen(int dtype, const void* cache, int64_t block_
  * No counterpart in the reference (it always has PyTorch allocate).
  * - num_seqs above NIB_NOALLOC_MAX_SEQS is rejected with NIB_ERR_INVALID.
  * - The first call on a device looks the array up (cudaGetSymbolAddress) with
- *   that device current; make that first call before any stream capture.
+ *   that device current; make that first call before any stream capture. The
+ *   address is kept per device together with the id of the CUDA context it
+ *   belongs to; after cudaDeviceReset the next call (again outside a capture)
+ *   sees the new context and looks the array up again.
  * - All calls on a device share the one array and each call rewrites it:
  *   calls whose kernels overlap on the GPU (different streams without ordering)
  *   race on it. Order them, e.g. issue them on one stream.
@@ -359,6 +362,24 @@ NIB_API int nib_deepstack_row_index(const int64_t* rows, int64_t n_rows, int64_t
  * _add_deepstack_rows (the clone at nanovllm/models/qwen3_vl.py:342). */
 NIB_API int nib_copy_rows(int dtype, const void* in, int64_t in_row_stride, int64_t rows, int64_t n,
                   void* out, int64_t out_row_stride, void* stream);
+
+/* ------------------------------------------------------------------ diagnostics */
+
+/* Status bit a kernel ORs into *status when one of its bounded bulk-copy
+ * waits (an mbarrier phase) gave up: the warp then waited, again bounded, for
+ * its other copies in flight and returned; its rows were not written. */
+#define NIB_DEV_TIMEOUT 16u
+
+/* Makes the library's bounded bulk-copy wait run out on purpose and returns:
+ * one warp arms an mbarrier for 32 bytes, lets a bulk copy bring 16 of them
+ * from src, waits at most limit_ns (1 us .. 2 s) of wall time, then sets
+ * NIB_DEV_TIMEOUT in *status, waits for its second (complete) 16-byte copy
+ * from src + 16 and writes *drained = 1 when that copy landed. This is the
+ * control flow of the pipelined attention prologue after a wait that gave up.
+ * src: 32 readable, 16-byte-aligned device bytes; status, drained: device words.
+ * No counterpart in the reference (it has no bounded device waits). */
+NIB_API int nib_selftest_bounded_wait(const void* src, int64_t limit_ns, unsigned int* status,
+                                      int* drained, void* stream);
 
 #ifdef __cplusplus
 }

@@ -11,7 +11,7 @@
 
 namespace nib {
 
-constexpr unsigned int kDevTimeout = 16u;      // status bit: an mbarrier wait gave up
+constexpr unsigned int kDevTimeout = NIB_DEV_TIMEOUT;  // status bit: an mbarrier wait gave up
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -65,13 +65,14 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Wait for phase `parity` of `bar` to complete, at most kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Wait for phase `parity` of `bar` to complete, at most `limit_ns` of wall time.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 0; it < (1u << 30); ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) return false;
+    if ((it & 255u) == 255u && global_ns() - t0 > limit_ns) return false;
   }
   return false;
 }

@@ -10,6 +10,8 @@
 // address and stride is 16-byte aligned (else 8/4/2). Out-of-range slots and
 // block ids are never dereferenced: they set a status bit (store skips the
 // token, gather writes a zero row).
+#include <cuda.h>
+
 #include <mutex>
 
 #include "copy_rows.cuh"
@@ -125,10 +127,46 @@ static int gather_impl(int dtype, const void* cache, int64_t block_stride, int64
 static __device__ __align__(256) int64_t g_gather_offsets[NIB_NOALLOC_MAX_SEQS + 1];
 
 static std::mutex g_offsets_mu;
-static int64_t* g_offsets_dev[64] = {};
 
-// Device address of g_gather_offsets for the current device (looked up once
-// per device, with that device current).
+// Per device: the address of g_gather_offsets and the id of the CUDA context
+// it was looked up in. A device reset destroys the context and unloads this
+// module; the next context loads it again, possibly at another address, so a
+// changed context id means the address is looked up again.
+struct OffsetsEntry {
+  unsigned long long ctx_id;
+  int64_t* ptr;
+};
+static OffsetsEntry g_offsets_dev[64] = {};
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Id of the calling thread's current context (0: none yet, or no driver entry
+// point). The driver functions come through cudaGetDriverEntryPoint, so the
+// library still links only the CUDA runtime.
+static unsigned long long current_ctx_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool resolved = false;
+  if (!resolved) {  // under g_offsets_mu
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault) == cudaSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault) == cudaSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(f);
+    resolved = true;
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_gather_offsets for the current device, looked up with
+// that device current: on the first call on a device, and again whenever the
+// device's context changed since (after cudaDeviceReset).
 static int offsets_table(int64_t** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
@@ -137,16 +175,20 @@ static int offsets_table(int64_t** out) {
     return NIB_ERR_CUDA;
   }
   std::lock_guard<std::mutex> lock(g_offsets_mu);
-  if (g_offsets_dev[dev] == nullptr) {
+  OffsetsEntry& entry = g_offsets_dev[dev];
+  unsigned long long ctx = current_ctx_id();
+  if (entry.ptr == nullptr || ctx == 0 || ctx != entry.ctx_id) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_gather_offsets);
     if (e != cudaSuccess || p == nullptr) {
       set_error("paged_gather_varlen_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
       return NIB_ERR_CUDA;
     }
-    g_offsets_dev[dev] = static_cast<int64_t*>(p);
+    if (ctx == 0) ctx = current_ctx_id();  // the lookup made the primary context current
+    entry.ptr = static_cast<int64_t*>(p);
+    entry.ctx_id = ctx;
   }
-  *out = g_offsets_dev[dev];
+  *out = entry.ptr;
   return NIB_OK;
 }
 

@@ -23,6 +23,21 @@ hot-path names that the decoder models import at module load:
   its sources; ``ModelRunner`` then runs unchanged with
   ``paged_kv_backend="cuda"``.
 
+With ``fused=True`` (the default) it also binds the fused forwards of
+``layers.fused_models`` into the reference's model classes, so the model code
+runs the fused kernels without being edited:
+
+* ``nanovllm.layers.attention.Attention`` -> this package's ``Attention`` (same
+  interface, plus ``forward_stored`` for K/V that a prologue already wrote)
+* ``Qwen3Attention.forward``, ``Qwen25VLAttention.forward``,
+  ``Qwen3VLAttention.forward``: one prologue launch (q/k norm, RoPE / M-RoPE,
+  paged K/V store) between the projections
+* ``Qwen3VLDecoderLayer.forward``, ``Qwen3VLLanguageModel.forward``: residual
+  adds and DeepStack rows folded into the norms
+
+``fused=False`` rebinds only the per-op names above (each reference op replaced
+by its kernel, the model code calling them one at a time).
+
 Call it before ``nanovllm.models.*`` is imported (the models bind the layer
 classes at import time); already-imported model modules are patched too when
 they hold the names. Returns the list of rebound ``module.attribute`` names.
@@ -77,10 +92,23 @@ def _targets():
 _MODEL_MODULES = ("nanovllm.models.qwen3", "nanovllm.models.qwen25_vl", "nanovllm.models.qwen3_vl")
 
 
-def install() -> list[str]:
-    from nano_vllm_multimodal_b200.layers import qwen3_vl
+def _fused_forwards():
+    from nano_vllm_multimodal_b200.layers import fused_models as fm
+    return {
+        "nanovllm.models.qwen3": {"Qwen3Attention": fm.qwen3_attention_forward},
+        "nanovllm.models.qwen25_vl": {"Qwen25VLAttention": fm.qwen25_vl_attention_forward},
+        "nanovllm.models.qwen3_vl": {"Qwen3VLAttention": fm.qwen3_vl_attention_forward,
+                                     "Qwen3VLDecoderLayer": fm.qwen3_vl_decoder_layer_forward,
+                                     "Qwen3VLLanguageModel": fm.qwen3_vl_language_model_forward},
+    }
+
+
+def install(fused: bool = True) -> list[str]:
+    from nano_vllm_multimodal_b200.layers import attention, qwen3_vl
 
     targets = _targets()
+    if fused:
+        targets["nanovllm.layers.attention"]["Attention"] = attention.Attention
     done = []
     for mod_name, names in targets.items():
         try:
@@ -104,4 +132,15 @@ def install() -> list[str]:
     if lm is not None and hasattr(lm, "Qwen3VLLanguageModel"):
         lm.Qwen3VLLanguageModel._add_deepstack_rows = staticmethod(qwen3_vl.add_deepstack_rows)
         done.append("nanovllm.models.qwen3_vl.Qwen3VLLanguageModel._add_deepstack_rows")
+    if fused:
+        for mod_name, classes in _fused_forwards().items():
+            try:
+                mod = importlib.import_module(mod_name)
+            except ImportError:
+                continue
+            for cls_name, forward in classes.items():
+                cls = getattr(mod, cls_name, None)
+                if cls is not None:
+                    cls.forward = forward
+                    done.append(f"{mod_name}.{cls_name}.forward")
     return done

@@ -16,7 +16,10 @@ written, so the caller's attention must skip its own store.
 
 from __future__ import annotations
 
+import sys
+
 import torch
+from torch import nn
 
 from nano_vllm_multimodal_b200 import ops
 from nano_vllm_multimodal_b200.layers.paged_kv.base import validate_store_inputs
@@ -26,6 +29,74 @@ def store_kvcache(key, value, k_cache, v_cache, slot_mapping) -> None:
     """Write this step's K/V rows into the paged caches (slot -1 = skip)."""
     validate_store_inputs(key, value, k_cache, v_cache, slot_mapping)
     ops.paged_store(key, value, k_cache, v_cache, slot_mapping)
+
+
+def _step_context():
+    """The runner's per-step ``Context`` (``nanovllm/utils/context.py``): the
+    model runner sets it before every forward, so attention reads the slot
+    mapping, sequence boundaries and block tables from there."""
+    from nanovllm.utils.context import get_context
+    return get_context()
+
+
+def _attention_kernels():
+    """The prefill / decode attention functions as ``nanovllm.layers.attention``
+    binds them now (``install()`` rebinds the decode one to this package's
+    kernel; tests of the reference may patch either)."""
+    ref = sys.modules.get("nanovllm.layers.attention")
+    varlen = getattr(ref, "flash_attn_varlen_func", None)
+    decode = getattr(ref, "flash_attn_with_kvcache", None)
+    if varlen is None:
+        from flash_attn import flash_attn_varlen_func as varlen
+    if decode is None:
+        decode = flash_attn_with_kvcache
+    return varlen, decode
+
+
+class Attention(nn.Module):
+    """Drop-in for ``nanovllm.layers.attention.Attention`` (``attention.py:36-132``).
+
+    Same constructor, the same ``k_cache``/``v_cache``/``paged_kv_backend``
+    attributes that ``ModelRunner.allocate_kv_cache`` assigns
+    (``model_runner.py:681-690``), and the same ``forward(q, k, v)``: store this
+    step's K/V (through the runner's backend when it set one, else this
+    package's store), then prefill attention over the packed sequences or
+    decode attention over the paged cache.
+
+    ``forward_stored(q, k, v)`` is the same step for callers whose fused
+    prologue has already written K/V into the caches.
+    """
+
+    def __init__(self, num_heads, head_dim, scale, num_kv_heads):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.scale = scale
+        self.num_kv_heads = num_kv_heads
+        self.k_cache = self.v_cache = torch.tensor([])
+        self.paged_kv_backend = None
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+        k_cache, v_cache = self.k_cache, self.v_cache
+        if k_cache.numel() and v_cache.numel():
+            slots = _step_context().slot_mapping
+            if self.paged_kv_backend is None:
+                store_kvcache(k, v, k_cache, v_cache, slots)
+            else:
+                self.paged_kv_backend.store(k, v, k_cache, v_cache, slots)
+        return self.forward_stored(q, k, v)
+
+    def forward_stored(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+        ctx = _step_context()
+        varlen, decode = _attention_kernels()
+        if ctx.is_prefill:
+            if ctx.block_tables is not None:  # prefix cache / chunked prefill: read history from the cache
+                k, v = self.k_cache, self.v_cache
+            return varlen(q, k, v, max_seqlen_q=ctx.max_seqlen_q, cu_seqlens_q=ctx.cu_seqlens_q,
+                          max_seqlen_k=ctx.max_seqlen_k, cu_seqlens_k=ctx.cu_seqlens_k,
+                          softmax_scale=self.scale, causal=True, block_table=ctx.block_tables)
+        return decode(q.unsqueeze(1), self.k_cache, self.v_cache, cache_seqlens=ctx.context_lens,
+                      block_table=ctx.block_tables, softmax_scale=self.scale, causal=True)
 
 
 def _rope_args(rotary_emb):

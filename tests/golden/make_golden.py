@@ -1,9 +1,10 @@
 """Generate the golden fixtures by running the reference's OWN modules on the CPU.
 
-Run in a container that has the NanoInfer source checkout (read-only) at
-``$NANOINFER_REF`` (the default is ``REF`` below):
+Run where the NanoInfer source checkout is available; point
+``$NANOINFER_REF`` at the directory that holds its ``nanovllm`` package (no
+default: the script refuses to run without it):
 
-    TORCHDYNAMO_DISABLE=1 python tests/golden/make_golden.py
+    NANOINFER_REF=<checkout> TORCHDYNAMO_DISABLE=1 python tests/golden/make_golden.py
 
 ``TORCHDYNAMO_DISABLE=1`` makes the reference's ``@torch.compile`` methods run
 their eager bodies (inductor cannot compile on this CPU image); the numerics
@@ -32,7 +33,9 @@ import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("NANOINFER_REF", "/root/reference"))
+if not os.environ.get("NANOINFER_REF"):
+    sys.exit("make_golden.py: set NANOINFER_REF to the NanoInfer checkout (the directory holding nanovllm/)")
+REF = Path(os.environ["NANOINFER_REF"])
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REF))
 

@@ -1,8 +1,7 @@
 """``integration.install()`` against the reference's own ``nanovllm`` package (CPU).
 
-Runs only where the NanoInfer source checkout is present (``$NANOINFER_REF``,
-default as in ``tests/golden/make_golden.py``); elsewhere, e.g. on the GPU box,
-it skips. Each check runs in a fresh interpreter, so the reference's modules
+Runs only where the NanoInfer package is importable: ``$NANOINFER_REF``, or an
+install in the git-ignored ``baseline/_ref``; elsewhere it skips. Each check runs in a fresh interpreter, so the reference's modules
 never enter this test session.
 
 It imports a reference model module before ``install()`` (the model binds the
@@ -21,10 +20,10 @@ from pathlib import Path
 import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
-REF = Path(os.environ.get("NANOINFER_REF", "/root/reference"))
+REF = Path(os.environ.get("NANOINFER_REF") or ROOT / "baseline" / "_ref")
 
 pytestmark = pytest.mark.skipif(not (REF / "nanovllm" / "__init__.py").is_file(),
-                                reason="reference checkout not present")
+                                reason=f"NanoInfer reference not importable from {REF}")
 
 SCRIPT = r"""
 import json, sys, types
