@@ -19,8 +19,15 @@ are out of scope: their outputs are fixed synthetic device tensors.
 ``e2e``    = the same through the layer-module API with the step's host inputs
              (initial hidden states, positions, slot mapping) copied from
              pinned memory and the final hidden states copied back each step.
-``--impl reference`` times the reference's CPU path (the oracle port of its
-PyTorch code) on the host cores, rank 0 only.
+``--impl reference`` times the reference's CPU path on the host cores, rank 0
+only: its own modules when an install is importable (``baseline/_ref`` or
+``$NANOINFER_REF``), else the oracle port, on a bounded sample of the C5 step
+extrapolated by per-token cost. The ``cpu_baseline`` leg of the GPU line is the
+same measurement.
+
+``configs`` = C1-C4 (the other BASELINE configs): each config's fused layer on
+the GPU (CUDA-graph replay, inputs rotated past the L2) next to the same layer
+on the CPU over the config's full token count.
 """
 
 from __future__ import annotations
@@ -82,6 +89,9 @@ def parse_args(argv=None):
     p.add_argument("--decode-requests", type=int, default=256,
                    help="requests of the decode-attention component (C2: 256)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    p.add_argument("--no-configs", action="store_true", help="skip the C1-C4 table")
+    p.add_argument("--config-cpu-seconds", type=float, default=2.0,
+                   help="CPU budget per config of the C1-C4 table")
     p.add_argument("--cache-blocks", type=int, default=CACHE_BLOCKS,
                    help="blocks of 256 slots per K/V cache per GPU (smaller only for profiler captures)")
     return p.parse_args(argv)
@@ -395,38 +405,7 @@ def load_traffic_table() -> dict[str, float]:
     return out
 
 
-# ------------------------------------------------------------------ CPU baseline (oracle port)
-
-
-def cpu_layer_sample(tokens: int, seed: int = 0):
-    """CPU inputs of one C5 fused layer over ``tokens`` tokens (256-block cache)."""
-    from nano_vllm_multimodal_b200 import workloads as W
-
-    seeds = W._Seeds(5, "cpu")
-    seeds.index = 900 + seed
-    n = lambda shape, mean=0.0, std=1.0: W._normal(seeds, shape, mean, std)  # noqa: E731
-    return {
-        "hidden": n((tokens, H)), "residual": n((tokens, H)), "qkv": n((tokens, (NQ + 2 * NKV) * D)),
-        "attn_out": n((tokens, H)), "gate_up": n((tokens, 2 * INTER)),
-        "w_in": n((H,), 1.0, 0.1), "w_post": n((H,), 1.0, 0.1),
-        "q_weight": n((D,), 1.0, 0.1), "k_weight": n((D,), 1.0, 0.1),
-        "positions": torch.randint(0, 32768, (3, tokens), generator=seeds()),
-        "slot_mapping": torch.randperm(256 * 256, generator=seeds())[:tokens].to(torch.int32),
-        "key_cache": torch.full((256, 256, NKV, D), -3.0, dtype=torch.bfloat16),
-        "value_cache": torch.full((256, 256, NKV, D), -3.0, dtype=torch.bfloat16),
-    }
-
-
-def cpu_layer(sample):
-    import oracle as O
-
-    O.qwen3_vl_fused_layer(
-        sample["hidden"], sample["residual"], sample["qkv"], sample["attn_out"], sample["gate_up"],
-        positions=sample["positions"], inv_freq=O.mrope_inv_freq(D, THETA), sections=SECTIONS,
-        w_in=sample["w_in"], w_post=sample["w_post"], q_weight=sample["q_weight"],
-        k_weight=sample["k_weight"], eps=EPS, num_heads=NQ, num_kv_heads=NKV, head_dim=D,
-        key_cache=sample["key_cache"], value_cache=sample["value_cache"],
-        slot_mapping=sample["slot_mapping"], inplace=True)
+# ------------------------------------------------------------------ CPU path of the reference
 
 
 def host_threads() -> int:
@@ -438,20 +417,69 @@ def host_threads() -> int:
     return n
 
 
-def cpu_baseline(budget_s: float, tokens: int = 2048) -> dict:
+CPU_SAMPLE_TOKENS = 2048
+
+
+def cpu_c5_sample():
+    """A bounded sample of the C5 step on the CPU: one fused layer over 2,048 C5
+    tokens (cache of 256 blocks, slots drawn from it) and one 16,384-token
+    sequence gathered from a 64-block table."""
+    from nano_vllm_multimodal_b200 import workloads as W
+    from oracle.cpu_layer import CpuLayer
+
+    d = W.make_layer_inputs(5, tokens=CPU_SAMPLE_TOKENS, cache=False)
+    seeds = W._Seeds(5, "cpu")
+    seeds.index = 950
+    d["slot_mapping"] = W._randperm(seeds, 256 * 256, CPU_SAMPLE_TOKENS)
+    d["key_cache"] = torch.full((256, 256, NKV, D), -3.0, dtype=torch.bfloat16)
+    d["value_cache"] = torch.full((256, 256, NKV, D), -3.0, dtype=torch.bfloat16)
+    d["table"] = W._randperm(seeds, 256, GATHER_LEN // 256)
+    return CpuLayer(W.C5, d), d
+
+
+def cpu_sample_step(layer, d):
+    """One sample step -> (layer seconds, gather seconds for K and V)."""
+    t0 = time.perf_counter()
+    layer(d)
+    t1 = time.perf_counter()
+    layer.gather(d["key_cache"], d["table"], GATHER_LEN)
+    layer.gather(d["value_cache"], d["table"], GATHER_LEN)
+    return t1 - t0, time.perf_counter() - t1
+
+
+def cpu_extrapolate(layer_s, gather_s, reps, tokens_total=TOKENS, layers=LAYERS):
+    """Per-token costs of the sample -> seconds of the whole C5 step and the metric."""
+    per_layer_token = layer_s / (reps * CPU_SAMPLE_TOKENS)
+    per_gather_token = gather_s / (reps * 2 * GATHER_LEN)
+    step_s = per_layer_token * tokens_total * layers + per_gather_token * 2 * GATHER_SEQS * GATHER_LEN
+    return step_s, tokens_total * layers / step_s
+
+
+def cpu_sample_desc(kind, reps, cores):
+    who = ("the reference's own modules (nanovllm.layers / models.qwen3_vl, PyTorch paged-KV backend, "
+           "eager: torch.compile disabled)" if kind == "reference" else "the oracle port of the reference's ops")
+    return (f"{reps} sample steps on {cores} host threads, each one fused C5 layer over {CPU_SAMPLE_TOKENS} "
+            f"tokens plus one {GATHER_LEN}-token sequence gathered from K and V, run by {who}; "
+            f"extrapolated by per-token cost to the C5 step ({TOKENS} tokens x {LAYERS} layers + "
+            f"{GATHER_SEQS} x {GATHER_LEN}-token K/V gather)")
+
+
+def cpu_baseline(budget_s: float) -> dict:
+    """The CPU figure on the GPU arm's line: the same measurement as ``--impl reference``."""
     cores = host_threads()
-    sample = cpu_layer_sample(tokens)
-    cpu_layer(sample)  # warm-up
+    layer, d = cpu_c5_sample()
+    cpu_sample_step(layer, d)  # warm-up
+    lt = gt = 0.0
     reps, t0 = 0, time.perf_counter()
     while True:
-        cpu_layer(sample)
-        reps += 1
-        el = time.perf_counter() - t0
-        if el >= budget_s:
+        a, b = cpu_sample_step(layer, d)
+        lt, gt, reps = lt + a, gt + b, reps + 1
+        if time.perf_counter() - t0 >= budget_s:
             break
-    return {"value": tokens * reps / el, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{reps} x one fused layer over {tokens} C5 tokens on the CPU oracle "
-                      f"(reference eager PyTorch ops), {el:.1f} s"}
+    step_s, value = cpu_extrapolate(lt, gt, reps)
+    return {"value": value, "unit": UNIT, "cores": cores, "kind": layer.kind,
+            "sample": cpu_sample_desc(layer.kind, reps, cores),
+            "extrapolated_step_s": round(step_s, 3)}
 
 
 def config_block(args, world, extra=None):
@@ -991,30 +1019,173 @@ def decode_layer_graph(device, config=2, layers=28, replays=50):
             "config": cfg + "; 28 layers per captured graph"}
 
 
+# ------------------------------------------------------------------ per-config table (C1-C4)
+L2_BYTES = 126 * 1024 * 1024
+
+
+def layer_bytes(shape, tokens: int, valid: int) -> int:
+    """Algorithmic bytes of one fused layer (2 x add+norm, prologue, SiluAndMul) over
+    ``tokens`` tokens of which ``valid`` have a cache slot."""
+    s = shape
+    axes = 1 if s.rope == "table" else 3
+    nq, nkv, hd = s.num_heads, s.num_kv_heads, s.head_dim
+    norms = 2 * 8 * s.hidden * tokens
+    prologue = tokens * (2 * ((nq + 2 * nkv) * hd + nq * hd + nkv * hd) + 8 * axes + 4) + valid * 2 * 2 * nkv * hd
+    return norms + prologue + 6 * s.intermediate * tokens
+
+
+def _rope_args(shape, device):
+    from nano_vllm_multimodal_b200 import ops
+    from nano_vllm_multimodal_b200.layers.multimodal_rotary_embedding import MultimodalRotaryEmbedding
+    from nano_vllm_multimodal_b200.layers.rotary_embedding import RotaryEmbedding
+
+    hd = shape.head_dim
+    if shape.rope == "table":
+        table = RotaryEmbedding(hd, hd, shape.max_position, shape.theta).to(device).cos_sin_cache
+        return dict(rope_mode=ops.ROPE_TABLE, cos_sin_cache=table)
+    mod = MultimodalRotaryEmbedding(head_dim=hd, base=shape.theta, sections=shape.sections,
+                                    strategy=shape.rope).to(device)
+    mode = ops.ROPE_MROPE_INTERLEAVED if shape.rope == "interleaved" else ops.ROPE_MROPE_CHUNKED
+    return dict(rope_mode=mode, inv_freq=mod.inv_freq, sections=shape.sections)
+
+
+def config_layer_gpu(config: int, device, hbm_peak: float, layers: int = 16, replays: int = 20,
+                     tokens: int | None = None) -> dict:
+    """One config's fused layer as the installed models run it (rounded add + text
+    norm for Qwen3-VL, fused add+norm otherwise; the prologue with the config's
+    q/k norm, rotary and store; SiluAndMul), ``layers`` layers captured in one CUDA
+    graph and replayed. The layers cycle over enough separate activation sets that
+    together they exceed 3x the L2, so bytes come from HBM."""
+    import math
+
+    from nano_vllm_multimodal_b200 import ops, workloads as W
+
+    d = W.make_layer_inputs(config, device=device, tokens=tokens, extras=False)
+    s, T = d["shape"], d["tokens"]
+    valid = int((d["slot_mapping"] >= 0).sum())
+    nbytes = layer_bytes(s, T, valid)
+    nsets = max(2, math.ceil(3 * L2_BYTES / nbytes))
+    keys = ("hidden", "residual", "qkv", "attn_out", "gate_up")
+    g = torch.Generator(device=device).manual_seed(4000 + config)
+    sets = [{k: d[k] for k in keys}] + [
+        {k: torch.randn(d[k].shape, generator=g, device=device).to(d[k].dtype) for k in keys}
+        for _ in range(nsets - 1)]
+    rope = _rope_args(s, device)
+    nq, nkv, hd = s.num_heads, s.num_kv_heads, s.head_dim
+    text = s.qk_norm == "text"
+    norm = dict(q_weight=d["q_weight"], k_weight=d["k_weight"], eps=s.eps) if s.qk_norm else {}
+    views = []
+    for a in sets:
+        q, k, v = a["qkv"].split([nq * hd, nkv * hd, nkv * hd], -1)
+        views.append((q.view(-1, nq, hd), k.view(-1, nkv, hd), v.view(-1, nkv, hd)))
+
+    def step():
+        for i in range(layers):
+            a, (q, k, v) = sets[i % nsets], views[i % nsets]
+            _, h1 = ops.add_rms_norm(a["hidden"], a["residual"], d["w_in"], s.eps, text)
+            ops.qk_prologue(q, k, v=v, positions=d["positions"], key_cache=d["key_cache"],
+                            value_cache=d["value_cache"], slot_mapping=d["slot_mapping"], **norm, **rope)
+            ops.add_rms_norm(a["attn_out"], h1, d["w_post"], s.eps, text)
+            ops.silu_and_mul(a["gate_up"])
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (replays * layers)
+    del graph
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"tokens": T, "us_per_layer": round(us, 3), "tokens_per_s": T / (us * 1e-6),
+            "bytes_per_layer": nbytes, "achieved_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4),
+            "input_sets": nsets, "launches_per_layer": 4, "layers_per_graph": layers}
+
+
+def config_layer_cpu(config: int, budget_s: float) -> dict:
+    """The same layer on the CPU over the config's full token count (the reference's
+    modules when importable, else the oracle port), repeated for about ``budget_s``."""
+    from nano_vllm_multimodal_b200 import workloads as W
+    from oracle.cpu_layer import CpuLayer
+
+    cores = host_threads()
+    d = W.make_layer_inputs(config, extras=False)
+    layer = CpuLayer(d["shape"], d)
+    layer(d)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        layer(d)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return {"cpu_tokens_per_s": d["tokens"] * reps / el, "cpu_kind": layer.kind, "cpu_cores": cores,
+            "cpu_reps": reps}
+
+
+CONFIG_NOTES = {
+    1: "C1 Qwen3-0.6B layer: 512 tokens, hidden 1024, 16/8 heads, q/k RMSNorm, 1-D RoPE theta 1e6, I=3072",
+    2: "C2 Qwen3-0.6B decode: 256 tokens, 10% slots -1, hidden 1024, 16/8 heads, 1-D RoPE, I=3072",
+    3: "C3 Qwen3-VL-2B prefill: 16 x 2048 tokens, hidden 2048, 16/8 heads, text norm, interleaved "
+       "M-RoPE [24,20,20] theta 5e6, I=6144",
+    4: "C4 Qwen2.5-VL-3B mixed chunked step: 8192 + 120 tokens, hidden 2048, 16/2 heads, no q/k norm, "
+       "chunked M-RoPE [16,24,24] theta 1e6, I=11008",
+}
+
+
+def config_table(device, hbm_peak: float, cpu_budget_s: float = 2.0) -> dict:
+    out = {}
+    for c in (1, 2, 3, 4):
+        row = {"config": CONFIG_NOTES[c]}
+        row.update(config_layer_gpu(c, device, hbm_peak))
+        torch.cuda.empty_cache()
+        if cpu_budget_s > 0:
+            row.update(config_layer_cpu(c, cpu_budget_s))
+            row["gpu_over_cpu"] = round(row["tokens_per_s"] / row["cpu_tokens_per_s"], 1)
+        out[f"C{c}"] = row
+    return out
+
+
 # ------------------------------------------------------------------ arms
 
 
 def reference_arm(args, rank, world):
+    """The reference's CPU path on the host cores (rank 0 only): the same sample
+    and extrapolation as the ``cpu_baseline`` leg of the GPU arm's line."""
     if rank != 0:
         return 0
     cores = host_threads()
-    tokens = 4096
-    sample = cpu_layer_sample(tokens)
-    for _ in range(args.warmup):
-        cpu_layer(sample)
-    times = []
+    layer, d = cpu_c5_sample()
+    for _ in range(max(1, args.warmup)):
+        cpu_sample_step(layer, d)
+    lt = gt = 0.0
     for _ in range(args.steps):
-        t0 = time.perf_counter()
-        cpu_layer(sample)
-        times.append(time.perf_counter() - t0)
-    total = sum(times)
-    value = tokens * args.steps / total
-    desc = f"one C5 fused layer over {tokens} tokens per step on {cores} host threads (oracle port)"
+        a, b = cpu_sample_step(layer, d)
+        lt, gt = lt + a, gt + b
+    step_s, value = cpu_extrapolate(lt, gt, args.steps, args.tokens, args.layers)
+    desc = cpu_sample_desc(layer.kind, args.steps, cores)
+    cfg = config_block(args, 1, {
+        "parallelism": "CPU, rank 0 only",
+        "cpu_sample": {"step": f"one fused layer over {CPU_SAMPLE_TOKENS} C5 tokens + one {GATHER_LEN}-token "
+                               "sequence gathered from K and V", "extrapolated_to": "the C5 step above, by "
+                               "per-token cost", "gather_included": True, "kind": layer.kind}})
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * (lt + gt) / args.steps,
+            "extrapolated_ms_per_c5_step": 1000 * step_s,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded, C5 shapes)", "config": config_block(args, 1),
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc},
+            "data": "synthetic (seeded, C5 shapes)", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": layer.kind, "sample": desc},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -1117,6 +1288,10 @@ def ours_arm(args, rank, world, local):
     if world == 1 and not args.no_components:
         components = component_bench(inp, device, hbm_peak)
 
+    configs = None
+    if world == 1 and not args.no_configs:
+        configs = config_table(device, hbm_peak, 0.0 if args.no_cpu_baseline else args.config_cpu_seconds)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_seconds)
@@ -1137,7 +1312,7 @@ def ours_arm(args, rank, world, local):
                 "gbs": step_bytes_job / (ms_max / args.steps / 1000.0) / 1e9,
                 "frac_of_peak": step_bytes_job / (ms_max / args.steps / 1000.0) / 1e9 / (hbm_peak * world),
                 "peak_gbs": hbm_peak * world, "peak_note": "measured per-GPU copy bandwidth x GPUs"},
-        "roofline": roofline, "kernels": per_kernel, "components": components,
+        "roofline": roofline, "kernels": per_kernel, "configs": configs, "components": components,
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clock,
         "gpu_launches": launches_per_step(args.layers, inp["gather_seqs"]) * args.steps,
     }

@@ -168,13 +168,14 @@ def deepstack_rows(config: int, tokens: int):
     return torch.tensor(rows, dtype=torch.int64)
 
 
-def make_layer_inputs(config: int, *, tokens: int | None = None, device="cpu", cache=True):
+def make_layer_inputs(config: int, *, tokens: int | None = None, device="cpu", cache=True, extras=True):
     """Inputs of one fused layer for config ``config`` (optionally truncated).
 
     Keys: ``hidden``, ``residual``, ``qkv``, ``attn_out``, ``gate_up``,
     ``positions``, ``slot_mapping``, ``key_cache``/``value_cache`` (prefilled
     with -3, as the reference's parity tests do), the four norm weights, and for
-    C2 ``embedding``/``token_ids``, for C3 ``deepstack`` rows and tensors.
+    C2 ``embedding``/``token_ids``, for C3 ``deepstack`` rows and tensors
+    (``extras=False`` leaves those out).
     """
     shape = CONFIGS[config]
     T = shape.tokens if tokens is None else tokens
@@ -198,11 +199,11 @@ def make_layer_inputs(config: int, *, tokens: int | None = None, device="cpu", c
         cshape = (shape.num_blocks, shape.block_size, shape.num_kv_heads, shape.head_dim)
         out["key_cache"] = torch.full(cshape, -3.0, dtype=BF16, device=device)
         out["value_cache"] = torch.full(cshape, -3.0, dtype=BF16, device=device)
-    if config == 2:
+    if config == 2 and extras:
         vocab = shape.extra["vocab"]
         out["embedding"] = _normal(seeds, (vocab, shape.hidden), 0.0, 0.02)
         out["token_ids"] = torch.randint(0, vocab, (T,), generator=seeds(), device=seeds.device)
-    if config == 3:
+    if config == 3 and extras:
         rows = deepstack_rows(3, T).to(device)
         out["deepstack_rows"] = rows
         out["deepstack"] = [_normal(seeds, (rows.numel(), shape.hidden)) for _ in range(3)]
