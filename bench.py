@@ -83,7 +83,7 @@ def parse_args(argv=None):
     p.add_argument("--no-components", action="store_true", help="skip the per-kernel extras")
     p.add_argument("--component",
                    choices=("decode_attention", "step_inputs", "mrope", "rows", "visual_merge", "paged_store",
-                            "head_norm"),
+                            "head_norm", "decode_layers", "configs"),
                    default=None,
                    help="run only this standalone component (one GPU) and print its JSON")
     p.add_argument("--decode-requests", type=int, default=256,
@@ -1389,6 +1389,11 @@ def component_only(name, decode_requests=256):
         ms = _time_op(flush=flush, fn=lambda: ops.rms_norm(q, w, EPS))
         record("rms_norm_heads", ms, T * NQ * D * 2 * 2, f"q-norm: [{T},{NQ},{D}] strided view of the qkv rows; "
                "one call at a time after an L2 flush")
+    elif name == "decode_layers":
+        out["c2_decode_layer_graph"] = decode_layer_graph(device, 2)
+        out["c3_decode_layer_graph"] = decode_layer_graph(device, 3)
+    elif name == "configs":
+        out.update(config_table(device, hbm_peak, 0.0))
     elif name == "mrope":
         inv = (1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).to(device)
         mrope_component(record, device, inv)

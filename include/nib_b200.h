@@ -208,7 +208,9 @@ typedef struct {
   const void* q; int64_t q_token_stride, q_head_stride;
   const void* k; int64_t k_token_stride, k_head_stride;
   const void* v; int64_t v_token_stride, v_head_stride; /* only read when storing */
-  /* outputs: contiguous [tokens, num_heads, head_dim], [tokens, num_kv_heads, head_dim] */
+  /* outputs: contiguous [tokens, num_heads, head_dim], [tokens, num_kv_heads, head_dim];
+     k_out may be NULL when storing: rotated k then goes to the key cache only
+     (decode and chunked-prefill attention read k from the cache) */
   void* q_out;
   void* k_out;
   /* per-head RMSNorm (0 = off) */

@@ -1,5 +1,6 @@
 // ABI plumbing: version, per-thread error message, launch status, SM count.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 
 #include "nib_common.cuh"
@@ -15,8 +16,26 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
+static thread_local cudaError_t g_launch_error = cudaSuccess;
+
+void note_launch_error(cudaError_t e) {
+  if (g_launch_error == cudaSuccess) g_launch_error = e;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("NIB_B200_PDL");
+    return !(v && (v[0] == '0' || v[0] == 'n' || v[0] == 'N' || v[0] == 'f' || v[0] == 'F'));
+  }();
+  return on;
+}
+
 int launch_status(const char* what) {
   cudaError_t e = cudaGetLastError();
+  if (g_launch_error != cudaSuccess) {
+    e = g_launch_error;
+    g_launch_error = cudaSuccess;
+  }
   if (e != cudaSuccess) {
     set_error("%s: kernel launch failed: %s", what, cudaGetErrorString(e));
     return NIB_ERR_CUDA;

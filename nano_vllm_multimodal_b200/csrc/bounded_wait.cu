@@ -18,6 +18,7 @@ __global__ void bounded_wait_selftest_kernel(const unsigned char* __restrict__ s
   __shared__ __align__(16) unsigned char buf[2][16];
   __shared__ __align__(8) uint64_t bars[2];
   const int lane = threadIdx.x & 31;
+  pdl_enter();
   if (lane == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
@@ -52,7 +53,7 @@ extern "C" int nib_selftest_bounded_wait(const void* src, int64_t limit_ns, unsi
   NIB_REQUIRE(reinterpret_cast<uintptr_t>(src) % 16 == 0, "selftest_bounded_wait: src must be 16-byte aligned");
   NIB_REQUIRE(limit_ns >= 1000 && limit_ns <= static_cast<int64_t>(kWaitLimitNs),
               "selftest_bounded_wait: limit_ns must be within [1 us, 2 s]");
-  bounded_wait_selftest_kernel<<<1, 32, 0, as_stream(stream)>>>(
+  ::nib::launch_k(bounded_wait_selftest_kernel, 1, 32, 0, as_stream(stream),
       static_cast<const unsigned char*>(src), static_cast<unsigned long long>(limit_ns), status,
       drained);
   return launch_status("selftest_bounded_wait");

@@ -121,6 +121,7 @@ __device__ __forceinline__ void merge_state(float& m, float& l, f2_t* acc, float
 template <typename T, int D, int HPW>
 __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeMinBlocks)
 decode_attention_kernel(const DecodeParams p) {
+  ::nib::pdl_enter();
   constexpr int V = kDecodeVecs;       // 16-byte vectors per lane and token
   constexpr int E = Elem<T>::kPerVec * V;  // elements per lane and token
   constexpr int P = E / 2;             // packed pairs per lane and token
@@ -358,6 +359,7 @@ decode_attention_kernel(const DecodeParams p) {
 template <typename T, int D>
 __global__ void __launch_bounds__(D)
 decode_combine_kernel(const DecodeParams p) {
+  ::nib::pdl_enter();
   constexpr int SW = D + 2;
   const int64_t bh = blockIdx.x;  // b * num_heads + h
   const int64_t b = bh / p.num_heads;
@@ -472,8 +474,8 @@ static int launch_decode(const nib_decode_attention_args& a, const DecodePlan& p
     }
     configured[dev] = static_cast<int>(pl.smem);
   }
-  kernel<<<grid, pl.warps * 32, pl.smem, st>>>(p);
-  if (pl.splits > 1) decode_combine_kernel<T, D><<<static_cast<unsigned>(a.batch * a.num_heads), D, 0, st>>>(p);
+  ::nib::launch_k(kernel, grid, pl.warps * 32, pl.smem, st, p);
+  if (pl.splits > 1) ::nib::launch_k(decode_combine_kernel<T, D>, static_cast<unsigned>(a.batch * a.num_heads), D, 0, st, p);
   return launch_status("decode_attention");
 }
 

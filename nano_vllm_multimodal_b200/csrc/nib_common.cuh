@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/nib_b200.h"
 
 namespace nib {
@@ -22,6 +24,43 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 // number of SMs of the current device (cached per device)
 int sm_count();
+
+// Programmatic dependent launch. Every kernel of this library is launched with
+// the programmatic-stream-serialization attribute (unless NIB_B200_PDL=0 in the
+// environment): it may be scheduled while the kernel before it on the stream
+// is still finishing, so its launch latency and block set-up overlap that
+// tail. Each kernel therefore starts with pdl_enter(), which waits for the
+// preceding grid to complete (and its memory to be visible) before touching
+// global memory, then lets the next kernel launch early in turn.
+bool pdl_enabled();
+void note_launch_error(cudaError_t e);  // reported by the next launch_status()
+
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) note_launch_error(e);
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// first statement of every kernel: wait for the predecessor grid, then allow the successor's launch
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_launch_dependents();
+}
 
 // Largest grid.x a one-shot launch uses; kernels grid-stride past it.
 constexpr int64_t kMaxGrid = 0x7fffffff;

@@ -49,6 +49,7 @@ __global__ void __launch_bounds__(256, G < 32 ? 2 : 1)
 rms_rows_warp(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __restrict__ res,
               int64_t r_rs, const W* __restrict__ w, T* __restrict__ y, T* __restrict__ res_out,
               int64_t rows, int64_t heads, int n, float eps, int add, int round_sum, DsArgs ds) {
+  ::nib::pdl_enter();
   // G lanes per row, VPT 16-byte vectors per lane, RB row batches per step
   // (all RB * VPT loads of a lane are issued before any math)
   constexpr int E = Elem<T>::kPerVec;
@@ -180,6 +181,7 @@ __global__ void __launch_bounds__(1024)
 rms_rows_block(const T* __restrict__ x, int64_t x_ts, int64_t x_hs, const T* __restrict__ res,
                int64_t r_rs, const W* __restrict__ w, T* __restrict__ y, T* __restrict__ res_out,
                int64_t rows, int64_t heads, int n, float eps, int add, int round_sum, DsArgs ds) {
+  ::nib::pdl_enter();
   constexpr int E = Elem<T>::kPerVec;
   __shared__ float red[32];
   const int nv = n / E;
@@ -277,13 +279,13 @@ static void launch_warp(const void* x, int64_t x_ts, int64_t x_hs, const void* r
   if (blocks < 1) blocks = 1;
   // a single wave of full-warp rows (decode batches) preloads the weights
   if (G == 32 && rows <= static_cast<int64_t>(sm_count()) * 4) {
-    rms_rows_warp<T, W, G, VPT, RB, DS, true><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+    ::nib::launch_k(rms_rows_warp<T, W, G, VPT, RB, DS, true>, static_cast<unsigned>(blocks), threads, 0, st,
         static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
         static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
         add, round_sum, ds);
     return;
   }
-  rms_rows_warp<T, W, G, VPT, RB, DS><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+  ::nib::launch_k(rms_rows_warp<T, W, G, VPT, RB, DS>, static_cast<unsigned>(blocks), threads, 0, st,
       static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
       static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
       add, round_sum, ds);
@@ -327,7 +329,7 @@ static int launch_rms(const void* x, int64_t x_ts, int64_t x_hs, const void* res
   const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / threads);
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  rms_rows_block<T, W, 4, DS><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+  ::nib::launch_k(rms_rows_block<T, W, 4, DS>, static_cast<unsigned>(blocks), threads, 0, st,
       static_cast<const T*>(x), x_ts, x_hs, static_cast<const T*>(res), r_rs,
       static_cast<const W*>(w), static_cast<T*>(y), static_cast<T*>(res_out), rows, heads, n, eps,
       add, round_sum, ds);

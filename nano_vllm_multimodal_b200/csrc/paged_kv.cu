@@ -25,6 +25,7 @@ paged_store_kernel(const char* __restrict__ key, int64_t kts, const char* __rest
                    int64_t vts, int64_t tokens, int units, char* __restrict__ kc,
                    char* __restrict__ vc, int64_t css, int64_t num_slots,
                    const int32_t* __restrict__ slots, unsigned int* status) {
+  ::nib::pdl_enter();
   using V = typename VecOf<VW>::type;
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -69,6 +70,7 @@ paged_gather_kernel(const char* __restrict__ cache, int64_t bst, int64_t sst, in
                     const int32_t* __restrict__ seq_lens, const int64_t* __restrict__ cu,
                     int64_t fixed_len, char* __restrict__ out, int64_t row_bytes,
                     unsigned int* status) {
+  ::nib::pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t seq = blockIdx.y;
   const int64_t len = seq_lens ? static_cast<int64_t>(__ldg(seq_lens + seq)) : fixed_len;
@@ -114,7 +116,7 @@ static int gather_impl(int dtype, const void* cache, int64_t block_stride, int64
   NIB_SUPPORT(num_seqs <= 65535, "paged gather: at most 65535 sequences per launch");
   dim3 grid(grid_for_rows(max_len, 8, 16), static_cast<unsigned>(num_seqs));
   NIB_VW_SWITCH(vw, VW,
-                paged_gather_kernel<VW><<<grid, 256, 0, st>>>(
+                ::nib::launch_k(paged_gather_kernel<VW>, grid, 256, 0, st,
                     static_cast<const char*>(cache), block_stride * es, slot_stride * es, num_blocks,
                     block_size, units, tables, table_stride, seq_lens, cu, max_len,
                     static_cast<char*>(out), row_bytes, status));
@@ -197,6 +199,7 @@ static int offsets_table(int64_t** out) {
 // nothing from an earlier call is ever read).
 __global__ void __launch_bounds__(1024)
 gather_offsets_kernel(const int32_t* __restrict__ lens, int n, int64_t* __restrict__ offsets) {
+  ::nib::pdl_enter();
   __shared__ int64_t warp_total[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int64_t v[4], local = 0;
@@ -263,7 +266,7 @@ extern "C" int nib_paged_store(int dtype, const void* key, int64_t key_token_str
   const cudaStream_t st = as_stream(stream);
   const unsigned grid = grid_for_rows(tokens, 8, 0);  // one-shot: 3% faster than 16 CTAs/SM
   NIB_VW_SWITCH(vw, VW,
-                paged_store_kernel<VW><<<grid, 256, 0, st>>>(
+                ::nib::launch_k(paged_store_kernel<VW>, grid, 256, 0, st,
                     static_cast<const char*>(key), key_token_stride * es,
                     static_cast<const char*>(value), value_token_stride * es, tokens, units,
                     static_cast<char*>(key_cache), static_cast<char*>(value_cache),
@@ -326,7 +329,7 @@ extern "C" int nib_paged_gather_varlen_noalloc(int dtype, const void* cache, int
   int rc = offsets_table(&offsets);
   if (rc != NIB_OK) return rc;
   const cudaStream_t st = as_stream(stream);
-  gather_offsets_kernel<<<1, 1024, 0, st>>>(seq_lens, static_cast<int>(num_seqs), offsets);
+  ::nib::launch_k(gather_offsets_kernel, 1, 1024, 0, st, seq_lens, static_cast<int>(num_seqs), offsets);
   rc = launch_status("paged_gather_varlen_noalloc (offsets)");
   if (rc != NIB_OK) return rc;
   return gather_impl(dtype, cache, block_stride, slot_stride, num_blocks, block_size, row_elems,

@@ -86,6 +86,7 @@ qk_prologue_pipe_kernel(const nib_qk_prologue_args a, const int stages, const ui
     fence_mbar_init();
   }
   __syncwarp();
+  pdl_enter();  // the barrier set-up above overlaps the previous kernel's tail
 
   // ---- per-lane constants: norm weights, M-RoPE frequency layout
   HeadWeights<T, W> wq, wk;
@@ -279,9 +280,11 @@ qk_prologue_pipe_kernel(const nib_qk_prologue_args a, const int stages, const ui
           st_vec(dst, oa);
           st_vec(dst + NF, ob);
         } else {
-          T* dst = k_out + ko_base + hoff[g];
-          st_vec(dst, oa);
-          st_vec(dst + NF, ob);
+          if (k_out) {
+            T* dst = k_out + ko_base + hoff[g];
+            st_vec(dst, oa);
+            st_vec(dst + NF, ob);
+          }
           if (kc_t) {
             st_vec(kc_t + hoff[g], oa);
             st_vec(kc_t + hoff[g] + NF, ob);
@@ -372,7 +375,7 @@ static int launch_pipe_d(const nib_qk_prologue_args& a, const PipeLayout& lay, c
   const int64_t by_tokens = (warps_needed + lay.warps - 1) / lay.warps;
   if (blocks > by_tokens) blocks = by_tokens;
   if (blocks < 1) blocks = 1;
-  kernel<<<static_cast<unsigned>(blocks), lay.warps * 32, lay.smem_bytes, st>>>(
+  ::nib::launch_k(kernel, static_cast<unsigned>(blocks), lay.warps * 32, lay.smem_bytes, st,
       a, lay.stages, lay.row_bytes, lay.stage_bytes);
   return launch_status("qk_prologue (pipelined)");
 }

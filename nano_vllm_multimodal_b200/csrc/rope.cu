@@ -41,6 +41,7 @@ constexpr int64_t kFewItems = 4096;
 template <typename T, typename W, int D, int CH>
 __global__ void __launch_bounds__(kPrologueWarps * 32)
 qk_prologue_kernel(const nib_qk_prologue_args a) {
+  ::nib::pdl_enter();
   constexpr int E = Elem<T>::kPerVec;
   constexpr int L = D / (2 * E);  // lanes per head (paired-halves layout)
   static_assert(L >= 1 && L <= 32, "head must span 1..32 lanes");
@@ -208,9 +209,11 @@ qk_prologue_kernel(const nib_qk_prologue_args a) {
         if (a.rope_mode != NIB_ROPE_NONE) rotate_pair<T>(xa, xb, wa, wb, c, s, c2, s2, inter);
         if (head_ok) {
           const uint4 oa = as_u4(wa), ob = as_u4(wb);
-          T* dst = is_q ? q_out + (t * nq + head) * D : k_out + (t * nkv + head) * D;
-          st_vec(dst + fb, oa);
-          st_vec(dst + NF + fb, ob);
+          T* dst = is_q ? q_out + (t * nq + head) * D : (k_out ? k_out + (t * nkv + head) * D : nullptr);
+          if (dst) {
+            st_vec(dst + fb, oa);
+            st_vec(dst + NF + fb, ob);
+          }
           if (!is_q && slot >= 0) {
             T* cd = kc + slot * a.cache_slot_stride + head * D;
             st_vec(cd + fb, oa);
@@ -238,6 +241,7 @@ __global__ void __launch_bounds__(256)
 mrope_apply_kernel(const TX* __restrict__ x, int64_t xts, int64_t xhs, int64_t tokens,
                    int64_t heads, int D, const TC* __restrict__ cos, const TC* __restrict__ sin,
                    int s0, int s1, int s2, int interleaved, TX* __restrict__ out) {
+  ::nib::pdl_enter();
   const int64_t total = tokens * heads * D;
   const int half = D / 2;
   for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
@@ -310,6 +314,7 @@ __global__ void __launch_bounds__(kApplyWarps * 32, INTER ? 6 : 4)
 mrope_apply_vec_kernel(const T* __restrict__ x, int64_t xts, int64_t xhs, int64_t tokens, int heads,
                        const T* __restrict__ cos, const T* __restrict__ sin, int s0, int s1, int s2,
                        T* __restrict__ out) {
+  ::nib::pdl_enter();
   constexpr int E = Elem<T>::kPerVec;
   constexpr int L = D / (2 * E);
   constexpr int HPW = 32 / L;
@@ -414,6 +419,7 @@ __global__ void __launch_bounds__(256)
 mrope_cos_sin_any_kernel(const int64_t* __restrict__ pos, int64_t pas, int64_t pts, int64_t tokens,
                      const float* __restrict__ inv_freq, int D, TO* __restrict__ cos,
                      TO* __restrict__ sin) {
+  ::nib::pdl_enter();
   const int half = D / 2;
   const int64_t total = 3 * tokens * half;
   for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
@@ -442,6 +448,7 @@ __global__ void __launch_bounds__(256)
 mrope_cos_sin_pair_kernel(const int64_t* __restrict__ pos, int64_t pas, int64_t pts, int64_t tokens,
                           const float* __restrict__ inv_freq, int D, TO* __restrict__ cos,
                           TO* __restrict__ sin) {
+  ::nib::pdl_enter();
   using P2 = typename Vec2<TO>::type;
   const int half = D / 2;
   const int hp = HP > 0 ? HP : half / 2;
@@ -504,8 +511,8 @@ static int launch_prologue(const nib_qk_prologue_args& a, cudaStream_t st) {
   const int threads = kPrologueWarps * 32;
   auto run = [&](auto dtag) {
     constexpr int DD = decltype(dtag)::value;
-    if (few) qk_prologue_kernel<T, W, DD, 1><<<nb, threads, 0, st>>>(a);
-    else qk_prologue_kernel<T, W, DD, kChunk><<<nb, threads, 0, st>>>(a);
+    if (few) ::nib::launch_k(qk_prologue_kernel<T, W, DD, 1>, nb, threads, 0, st, a);
+    else ::nib::launch_k(qk_prologue_kernel<T, W, DD, kChunk>, nb, threads, 0, st, a);
   };
   if (D == 64) run(std::integral_constant<int, 64>{});
   else if (D == 128) run(std::integral_constant<int, 128>{});
@@ -525,9 +532,10 @@ extern "C" int nib_qk_prologue(const nib_qk_prologue_args* args, void* stream) {
   const nib_qk_prologue_args& a = *args;
   NIB_REQUIRE(a.tokens >= 0 && a.num_heads >= 1 && a.num_kv_heads >= 1, "qk_prologue: bad sizes");
   if (a.tokens == 0) return NIB_OK;
-  NIB_REQUIRE(a.q && a.k && a.q_out && a.k_out, "qk_prologue: null q/k pointer");
+  NIB_REQUIRE(a.q && a.k && a.q_out, "qk_prologue: null q/k pointer");
   const int E = 16 / elem_size(a.dtype);
   const bool store = a.key_cache != nullptr;
+  NIB_REQUIRE(a.k_out || store, "qk_prologue: k_out may be NULL only when storing into the caches");
   NIB_REQUIRE(!store || (a.value_cache && a.v && a.slot_mapping), "qk_prologue: store needs v, caches and slot_mapping");
   NIB_REQUIRE(!a.norm || (a.q_weight && a.k_weight), "qk_prologue: norm needs q/k weights");
   NIB_REQUIRE(a.rope_mode >= NIB_ROPE_NONE && a.rope_mode <= NIB_ROPE_MROPE_INTERLEAVED, "qk_prologue: bad rope mode");
@@ -539,7 +547,7 @@ extern "C" int nib_qk_prologue(const nib_qk_prologue_args* args, void* stream) {
                     a.sections[0] + a.sections[1] + a.sections[2] == a.head_dim / 2,
                 "qk_prologue: sections must be positive and sum to head_dim/2");
   }
-  const void* vec_ptrs[] = {a.q, a.k, a.q_out, a.k_out, store ? a.v : a.q,
+  const void* vec_ptrs[] = {a.q, a.k, a.q_out, a.k_out ? a.k_out : a.q, store ? a.v : a.q,
                             store ? a.key_cache : a.q, store ? a.value_cache : a.q};
   for (const void* p : vec_ptrs) NIB_SUPPORT(aligned16(p), "qk_prologue: tensors must be 16-byte aligned");
   const int64_t strides[] = {a.q_token_stride, a.q_head_stride, a.k_token_stride, a.k_head_stride,
@@ -591,7 +599,7 @@ extern "C" int nib_mrope_apply(int x_dtype, const void* x, int64_t x_token_strid
         constexpr int DD = decltype(dtag)::value;                                                  \
         auto kern = interleaved ? mrope_apply_vec_kernel<TT, DD, true>                             \
                                 : mrope_apply_vec_kernel<TT, DD, false>;                           \
-        kern<<<nb, th, 0, st>>>(                                                                   \
+        ::nib::launch_k(kern, nb, th, 0, st,                                                                    \
             static_cast<const TT*>(x), x_token_stride, x_head_stride, tokens, static_cast<int>(heads), \
             static_cast<const TT*>(cos), static_cast<const TT*>(sin), sections[0], sections[1],   \
             sections[2], static_cast<TT*>(out));                                                  \
@@ -605,7 +613,7 @@ extern "C" int nib_mrope_apply(int x_dtype, const void* x, int64_t x_token_strid
     return launch_status("mrope_apply");
   }
 #define NIB_MROPE_APPLY(TX, TC, TO)                                                              \
-  mrope_apply_kernel<TX, TC, TO><<<grid, 256, 0, st>>>(                                          \
+  ::nib::launch_k(mrope_apply_kernel<TX, TC, TO>, grid, 256, 0, st,                                           \
       static_cast<const TX*>(x), x_token_stride, x_head_stride, tokens, heads, D,                \
       static_cast<const TC*>(cos), static_cast<const TC*>(sin), sections[0], sections[1],        \
       sections[2], interleaved, static_cast<TX*>(out))
@@ -645,7 +653,7 @@ extern "C" int nib_mrope_cos_sin(const int64_t* positions, int64_t positions_axi
     const dim3 grid(static_cast<unsigned>(blocks), 3);
 #define NIB_COS_SIN_PAIR(HP)                                                                    \
   NIB_DISPATCH(out_dtype, TO,                                                                   \
-               mrope_cos_sin_pair_kernel<TO, HP><<<grid, 256, 0, st>>>(                         \
+               ::nib::launch_k(mrope_cos_sin_pair_kernel<TO, HP>, grid, 256, 0, st,                          \
                    positions, positions_axis_stride, positions_token_stride, tokens, inv_freq, D, \
                    static_cast<TO*>(cos), static_cast<TO*>(sin)))
     if (D == 64) {
@@ -662,7 +670,7 @@ extern "C" int nib_mrope_cos_sin(const int64_t* positions, int64_t positions_axi
   }
   const unsigned grid = flat_grid(3 * tokens * (head_dim / 2), 16);
   NIB_DISPATCH(out_dtype, TO,
-               mrope_cos_sin_any_kernel<TO><<<grid, 256, 0, st>>>(
+               ::nib::launch_k(mrope_cos_sin_any_kernel<TO>, grid, 256, 0, st,
                    positions, positions_axis_stride, positions_token_stride, tokens, inv_freq, D,
                    static_cast<TO*>(cos), static_cast<TO*>(sin)));
   return launch_status("mrope_cos_sin");

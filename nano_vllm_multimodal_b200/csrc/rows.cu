@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(256)
 embedding_kernel(const int64_t* __restrict__ ids, int64_t n_ids, const char* __restrict__ weight,
                  int64_t w_rs, int64_t vocab_rows, int64_t vstart, int64_t vend, int units,
                  int mask, char* __restrict__ out, int64_t row_bytes, unsigned int* status) {
+  ::nib::pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -38,6 +39,7 @@ embedding_kernel(const int64_t* __restrict__ ids, int64_t n_ids, const char* __r
 // index[t] = -1 for every token, then index[rows[j]] = j (two launches on one stream)
 __global__ void __launch_bounds__(256)
 fill_index_kernel(int32_t* __restrict__ index, int64_t tokens) {
+  ::nib::pdl_enter();
   for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < tokens;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x)
     index[t] = -1;
@@ -45,6 +47,7 @@ fill_index_kernel(int32_t* __restrict__ index, int64_t tokens) {
 __global__ void __launch_bounds__(256)
 scatter_index_kernel(const int64_t* __restrict__ rows, int64_t n_rows, int64_t tokens,
                      int32_t* __restrict__ index, unsigned int* status) {
+  ::nib::pdl_enter();
   for (int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < n_rows;
        j += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = __ldg(rows + j);
@@ -61,6 +64,7 @@ __global__ void __launch_bounds__(256)
 deepstack_add_kernel(T* __restrict__ h, int64_t h_rs, int64_t tokens, int n,
                      const int64_t* __restrict__ rows, int64_t n_rows, const T* __restrict__ vis,
                      int64_t v_rs, unsigned int* status) {
+  ::nib::pdl_enter();
   constexpr int E = Elem<T>::kPerVec;
   const int lane = threadIdx.x & 31;
   const int nv = n / E;
@@ -103,6 +107,7 @@ template <int VW>
 __global__ void __launch_bounds__(256)
 copy_rows_kernel(const char* __restrict__ in, int64_t in_rs, int64_t rows, int units,
                  char* __restrict__ out, int64_t out_rs) {
+  ::nib::pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -138,7 +143,7 @@ extern "C" int nib_embedding(int dtype, const int64_t* ids, int64_t n_ids, const
   const int units = static_cast<int>(row_bytes / vw);
   const cudaStream_t st = as_stream(stream);
   NIB_VW_SWITCH(vw, VW,
-                embedding_kernel<VW><<<warp_grid(n_ids), 256, 0, st>>>(
+                ::nib::launch_k(embedding_kernel<VW>, warp_grid(n_ids), 256, 0, st,
                     ids, n_ids, static_cast<const char*>(weight), weight_row_stride * es,
                     vocab_rows, vocab_start, vocab_end, units, mask_out_of_range,
                     static_cast<char*>(out), row_bytes, status));
@@ -157,7 +162,7 @@ extern "C" int nib_deepstack_add(int dtype, void* hidden, int64_t hidden_row_str
               "deepstack_add: row length and strides must be multiples of %d elements", E);
   const cudaStream_t st = as_stream(stream);
   NIB_DISPATCH(dtype, T,
-               deepstack_add_kernel<T><<<warp_grid(n_rows), 256, 0, st>>>(
+               ::nib::launch_k(deepstack_add_kernel<T>, warp_grid(n_rows), 256, 0, st,
                    static_cast<T*>(hidden), hidden_row_stride, tokens, static_cast<int>(n), rows,
                    n_rows, static_cast<const T*>(vis), vis_row_stride, status));
   return launch_status("deepstack_add");
@@ -171,11 +176,11 @@ extern "C" int nib_deepstack_row_index(const int64_t* rows, int64_t n_rows, int6
   const cudaStream_t st = as_stream(stream);
   int64_t blocks = (tokens + 255) / 256;
   if (blocks > kMaxGrid) blocks = kMaxGrid;
-  fill_index_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(index, tokens);
+  ::nib::launch_k(fill_index_kernel, static_cast<unsigned>(blocks), 256, 0, st, index, tokens);
   if (n_rows > 0) {
     int64_t b2 = (n_rows + 255) / 256;
     if (b2 > kMaxGrid) b2 = kMaxGrid;
-    scatter_index_kernel<<<static_cast<unsigned>(b2), 256, 0, st>>>(rows, n_rows, tokens, index, status);
+    ::nib::launch_k(scatter_index_kernel, static_cast<unsigned>(b2), 256, 0, st, rows, n_rows, tokens, index, status);
   }
   return launch_status("deepstack_row_index");
 }
@@ -195,7 +200,7 @@ extern "C" int nib_copy_rows(int dtype, const void* in, int64_t in_row_stride, i
   const int units = static_cast<int>(row_bytes / vw);
   const cudaStream_t st = as_stream(stream);
   NIB_VW_SWITCH(vw, VW,
-                copy_rows_kernel<VW><<<warp_grid(rows), 256, 0, st>>>(
+                ::nib::launch_k(copy_rows_kernel<VW>, warp_grid(rows), 256, 0, st,
                     static_cast<const char*>(in), in_row_stride * es, rows, units,
                     static_cast<char*>(out), out_row_stride * es));
   return launch_status("copy_rows");

@@ -68,6 +68,7 @@ constexpr int silu_min_blocks() { return KU <= 3 ? 4 : (KU == 4 ? 3 : (KU <= 6 ?
 template <typename T, int KU>
 __global__ void __launch_bounds__(256, silu_min_blocks<KU>())
 silu_mul_rows(const T* __restrict__ x, int64_t x_rs, T* __restrict__ y, int64_t rows, int inter) {
+  ::nib::pdl_enter();
   constexpr int E = Elem<T>::kPerVec;
   const int upr = inter / E;
   const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.y;
@@ -112,7 +113,7 @@ static int launch_silu(const void* x, int64_t x_rs, int64_t rows, int64_t inter,
   const dim3 block(tx, ty);
   switch (ku) {
 #define NIB_SILU_KU(K) \
-    case K: silu_mul_rows<T, K><<<nb, block, 0, st>>>(xp, x_rs, yp, rows, static_cast<int>(inter)); break;
+    case K: ::nib::launch_k(silu_mul_rows<T, K>, nb, block, 0, st, xp, x_rs, yp, rows, static_cast<int>(inter)); break;
     NIB_SILU_KU(1) NIB_SILU_KU(2) NIB_SILU_KU(3) NIB_SILU_KU(4)
     NIB_SILU_KU(5) NIB_SILU_KU(6) NIB_SILU_KU(7) NIB_SILU_KU(8)
 #undef NIB_SILU_KU

@@ -18,8 +18,8 @@
 #include <torch/library.h>
 
 #include <algorithm>
+#include <array>
 #include <cstring>
-#include <deque>
 #include <functional>
 #include <limits>
 #include <string>
@@ -156,7 +156,7 @@ std::tuple<Tensor, Tensor> qk_prologue(const Tensor& q, const Tensor& k, const o
                                        const optional<Tensor>& key_cache,
                                        const optional<Tensor>& value_cache,
                                        const optional<Tensor>& slot_mapping,
-                                       const optional<Tensor>& status, int64_t variant) {
+                                       const optional<Tensor>& status, int64_t variant, bool emit_k) {
   TORCH_CHECK(q.dim() == 3 && k.dim() == 3, "qk_prologue: q and k must be [tokens, heads, head_dim]");
   TORCH_CHECK(q.size(0) == k.size(0) && q.size(2) == k.size(2), "qk_prologue: q/k shape mismatch");
   TORCH_CHECK(q.scalar_type() == k.scalar_type(), "qk_prologue: q and k dtypes differ");
@@ -167,7 +167,11 @@ std::tuple<Tensor, Tensor> qk_prologue(const Tensor& q, const Tensor& k, const o
     if (t->has_value()) on_device(q, **t, "qk_prologue argument");
   c10::cuda::CUDAGuard guard(q.device());
   Tensor qo = at::empty(q.sizes(), q.options().memory_format(at::MemoryFormat::Contiguous));
-  Tensor ko = at::empty(k.sizes(), k.options().memory_format(at::MemoryFormat::Contiguous));
+  TORCH_CHECK(emit_k || key_cache.has_value(), "qk_prologue: emit_k=False needs the caches (rotated k goes only there)");
+  // emit_k=False: rotated k is written to the key cache only (decode and
+  // chunked prefill read k from the cache); the second result is then empty
+  Tensor ko = emit_k ? at::empty(k.sizes(), k.options().memory_format(at::MemoryFormat::Contiguous))
+                     : at::empty({0}, k.options());
   if (q.size(0) == 0) return {qo, ko};
   nib_qk_prologue_args a{};
   a.struct_size = sizeof(nib_qk_prologue_args);
@@ -179,7 +183,7 @@ std::tuple<Tensor, Tensor> qk_prologue(const Tensor& q, const Tensor& k, const o
   a.q = q.data_ptr(); a.q_token_stride = q.stride(0); a.q_head_stride = q.stride(1);
   a.k = k.data_ptr(); a.k_token_stride = k.stride(0); a.k_head_stride = k.stride(1);
   a.q_out = qo.data_ptr();
-  a.k_out = ko.data_ptr();
+  a.k_out = emit_k ? ko.data_ptr() : nullptr;
   Tensor qw, kw;
   if (q_weight.has_value()) {
     TORCH_CHECK(k_weight.has_value(), "qk_prologue: q_weight without k_weight");
@@ -572,110 +576,122 @@ at::ScalarType parse_dtype(const std::string& name) {
   TORCH_CHECK(false, "PagedKVCache does not support dtype ", name);
 }
 
-// Owns one cudaMalloc'd cache allocation plus a device buffer for the step's
-// slot mapping, refilled from pinned host memory on a private transfer stream
-// (semantics of csrc/paged_kv/paged_kv.cpp:41-179).
+// Owns one cudaMalloc'd cache allocation and the device buffer that receives
+// each step's slot mapping (the interface of the reference's runtime owner,
+// csrc/paged_kv/paged_kv.cpp:41-179: tensor(), copy_slots_async(),
+// pending_host_copy_count(); the same checks and messages).
+//
+// The slot mapping is copied on the caller's current stream. The reference
+// copies on a private transfer stream and orders it with two events each step
+// (the transfer waits for the compute stream, the compute stream waits for the
+// transfer), so nothing overlaps anyway; one copy in stream order gives the
+// same ordering with no cross-stream events: the previous step's kernels on
+// this stream finish reading the buffer before it is refilled, and this
+// step's kernels start after the copy landed.
+//
+// The pinned source must stay alive until its copy has run. Each call records
+// one event of a fixed ring (created once, here in the constructor) behind its
+// copy and keeps the source in that ring entry; entries whose event has
+// completed are released at the start of the next call. A full ring (the host
+// more than kRing steps ahead of the GPU) waits for its oldest copy.
 class PagedKVCache : public torch::CustomClassHolder {
  public:
+  static constexpr int kRing = 16;
+
   PagedKVCache(std::vector<int64_t> sizes, std::string dtype_name, int64_t device_index)
-      : sizes_(std::move(sizes)), device_(device_index) {
+      : device_(device_index) {
     TORCH_CHECK(device_ >= 0, "CUDA device index must be non-negative");
-    TORCH_CHECK(!sizes_.empty(), "PagedKVCache shape must not be empty");
+    TORCH_CHECK(!sizes.empty(), "PagedKVCache shape must not be empty");
     const at::ScalarType dtype = parse_dtype(dtype_name);
     int64_t numel = 1;
-    for (int64_t s : sizes_) {
+    for (int64_t s : sizes) {
       TORCH_CHECK(s > 0, "PagedKVCache dimensions must be positive");
       TORCH_CHECK(numel <= std::numeric_limits<int64_t>::max() / s, "PagedKVCache shape overflows int64");
       numel *= s;
     }
     c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device_));
-    void* p = nullptr;
-    NIB_CUDA_CHECK(cudaMalloc(&p, static_cast<size_t>(numel) * c10::elementSize(dtype)));
-    tensor_ = at::from_blob(p, sizes_, make_deleter(),
-                            at::TensorOptions().dtype(dtype).device(at::kCUDA, device_));
-    NIB_CUDA_CHECK(cudaStreamCreateWithFlags(&transfer_, cudaStreamNonBlocking));
-    NIB_CUDA_CHECK(cudaEventCreateWithFlags(&copied_, cudaEventDisableTiming));
-    NIB_CUDA_CHECK(cudaEventCreateWithFlags(&consumed_, cudaEventDisableTiming));
+    cache_ = owned_device_tensor(static_cast<size_t>(numel) * c10::elementSize(dtype), sizes, dtype);
+    for (Pending& p : ring_) NIB_CUDA_CHECK(cudaEventCreateWithFlags(&p.copied, cudaEventDisableTiming));
   }
 
   ~PagedKVCache() override {
     c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device_));
-    if (transfer_) cudaStreamSynchronize(transfer_);
-    for (auto& h : inflight_) cudaEventDestroy(h.done);
-    inflight_.clear();
-    if (copied_) cudaEventDestroy(copied_);
-    if (consumed_) cudaEventDestroy(consumed_);
-    if (transfer_) cudaStreamDestroy(transfer_);
+    for (Pending& p : ring_) {
+      if (p.source.defined()) cudaEventSynchronize(p.copied);  // a source must outlive its copy
+      p.source.reset();
+      if (p.copied) cudaEventDestroy(p.copied);
+    }
   }
 
-  Tensor tensor() const { return tensor_; }
-  int64_t pending_host_copy_count() const { return static_cast<int64_t>(inflight_.size()); }
+  Tensor tensor() const { return cache_; }
+
+  int64_t pending_host_copy_count() const { return live_; }
 
   Tensor copy_slots_async(const Tensor& host) {
     TORCH_CHECK(host.device().is_cpu(), "slot mapping source must be a CPU tensor");
     TORCH_CHECK(host.scalar_type() == at::kInt, "slot mapping source must be int32");
     TORCH_CHECK(host.dim() == 1 && host.is_contiguous(), "slot mapping source must be contiguous and one-dimensional");
     c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device_));
-    retire_finished();
-    const auto opts = at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device_);
+    release_landed();
     const int64_t n = host.numel();
-    if (n == 0) return at::empty({0}, opts);
+    if (n == 0) return at::empty({0}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device_));
     TORCH_CHECK(host.is_pinned(), "slot mapping source must use pinned CPU memory");
-    if (capacity_ < n) {
-      void* p = nullptr;
-      NIB_CUDA_CHECK(cudaMalloc(&p, static_cast<size_t>(n) * sizeof(int32_t)));
-      slots_ = at::from_blob(p, {n}, make_deleter(), opts);
-      capacity_ = n;
+    if (slots_.numel() < n) {
+      // grown only when a step has more tokens than any before; the old buffer
+      // is freed by its deleter once no tensor refers to it
+      slots_ = owned_device_tensor(static_cast<size_t>(n) * sizeof(int32_t), {n}, at::kInt);
     }
-    cudaStream_t compute = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(device_)).stream();
-    // the previous step's kernels must be done reading the buffer before it is refilled
-    NIB_CUDA_CHECK(cudaEventRecord(consumed_, compute));
-    NIB_CUDA_CHECK(cudaStreamWaitEvent(transfer_, consumed_, 0));
-    NIB_CUDA_CHECK(cudaMemcpyAsync(slots_.data_ptr(), host.data_ptr(), n * sizeof(int32_t),
-                                   cudaMemcpyHostToDevice, transfer_));
-    cudaEvent_t done = nullptr;
-    NIB_CUDA_CHECK(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
-    NIB_CUDA_CHECK(cudaEventRecord(done, transfer_));
-    inflight_.push_back({host, done});  // keeps the pinned source alive until the copy lands
-    NIB_CUDA_CHECK(cudaEventRecord(copied_, transfer_));
-    NIB_CUDA_CHECK(cudaStreamWaitEvent(compute, copied_, 0));
+    Pending& p = ring_[next_];
+    if (p.source.defined()) {  // ring full: the oldest copy must land before its entry is reused
+      NIB_CUDA_CHECK(cudaEventSynchronize(p.copied));
+      p.source.reset();
+      --live_;
+    }
+    const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(device_)).stream();
+    NIB_CUDA_CHECK(cudaMemcpyAsync(slots_.data_ptr(), host.data_ptr(), static_cast<size_t>(n) * sizeof(int32_t),
+                                   cudaMemcpyHostToDevice, stream));
+    NIB_CUDA_CHECK(cudaEventRecord(p.copied, stream));
+    p.source = host;
+    ++live_;
+    next_ = (next_ + 1) % kRing;
     return slots_.narrow(0, 0, n);
   }
 
  private:
-  struct HostCopy {
-    Tensor source;
-    cudaEvent_t done;
+  struct Pending {
+    Tensor source;            // the pinned host tensor, kept until `copied` completes
+    cudaEvent_t copied = nullptr;
   };
 
-  std::function<void(void*)> make_deleter() const {
+  Tensor owned_device_tensor(size_t bytes, at::IntArrayRef sizes, at::ScalarType dtype) const {
+    void* p = nullptr;
+    NIB_CUDA_CHECK(cudaMalloc(&p, bytes));
     const int64_t dev = device_;
-    return [dev](void* p) {
-      if (p == nullptr) return;
+    return at::from_blob(p, sizes, [dev](void* q) {
+      if (q == nullptr) return;
       c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(dev));
-      cudaFree(p);
-    };
+      cudaFree(q);
+    }, at::TensorOptions().dtype(dtype).device(at::kCUDA, device_));
   }
 
-  void retire_finished() {
-    while (!inflight_.empty()) {
-      const cudaError_t st = cudaEventQuery(inflight_.front().done);
+  // release, oldest first, every source whose copy has landed
+  void release_landed() {
+    for (int i = 0; i < kRing && live_ > 0; ++i) {
+      Pending& p = ring_[(next_ + kRing - live_) % kRing];
+      const cudaError_t st = cudaEventQuery(p.copied);
       if (st == cudaErrorNotReady) return;
       NIB_CUDA_CHECK(st);
-      NIB_CUDA_CHECK(cudaEventDestroy(inflight_.front().done));
-      inflight_.pop_front();
+      p.source.reset();
+      --live_;
     }
   }
 
-  std::vector<int64_t> sizes_;
   int64_t device_;
-  Tensor tensor_;
+  Tensor cache_;
   Tensor slots_;
-  int64_t capacity_ = 0;
-  cudaStream_t transfer_ = nullptr;
-  cudaEvent_t copied_ = nullptr;
-  cudaEvent_t consumed_ = nullptr;
-  std::deque<HostCopy> inflight_;
+  std::array<Pending, kRing> ring_{};
+  int next_ = 0;   // ring entry of the next copy
+  int live_ = 0;   // entries holding a source: the oldest is next_ - live_
 };
 
 // A step's host inputs (token ids, positions, slot mapping, cu_seqlens, ...;
@@ -815,7 +831,7 @@ TORCH_LIBRARY(nanoinfer_b200, m) {
   m.def("qk_prologue(Tensor q, Tensor k, Tensor? v, Tensor? positions, Tensor? q_weight, "
         "Tensor? k_weight, float eps, int rope_mode, Tensor? cos_sin_cache, Tensor? inv_freq, "
         "int[] sections, Tensor(a!)? key_cache, Tensor(b!)? value_cache, Tensor? slot_mapping, "
-        "Tensor(c!)? status, int variant=0) -> (Tensor, Tensor)");
+        "Tensor(c!)? status, int variant=0, bool emit_k=True) -> (Tensor, Tensor)");
   m.def("mrope_apply(Tensor x, Tensor cos, Tensor sin, int[] sections, bool interleaved) -> Tensor");
   m.def("mrope_cos_sin(Tensor positions, Tensor inv_freq, ScalarType dtype) -> (Tensor, Tensor)");
   m.def("paged_gather_varlen(Tensor cache, Tensor block_tables, Tensor seq_lens, Tensor cu_seqlens, "

@@ -71,6 +71,7 @@ __device__ __forceinline__ const nib_visual_source* resolve(const nib_visual_sou
 
 __global__ void __launch_bounds__(256)
 visual_row_map_fill(int32_t* __restrict__ row_map, int64_t tokens) {
+  ::nib::pdl_enter();
   for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < tokens;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x)
     row_map[t] = -1;
@@ -79,6 +80,7 @@ visual_row_map_fill(int32_t* __restrict__ row_map, int64_t tokens) {
 __global__ void __launch_bounds__(256)
 visual_row_map_scatter(const int64_t* __restrict__ output_rows, int64_t n, int64_t tokens,
                        int32_t* __restrict__ row_map, unsigned int* status) {
+  ::nib::pdl_enter();
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = __ldg(output_rows + i);
@@ -97,6 +99,7 @@ visual_merge_kernel(const char* __restrict__ tok, int64_t tok_rs_bytes, int64_t 
                     const int64_t* __restrict__ feature_rows, int64_t R,
                     const int32_t* __restrict__ row_map, char* __restrict__ merged,
                     char* __restrict__ deepstack, unsigned int* status) {
+  ::nib::pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t row_bytes = n * dtype_bytes(dd);
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -157,12 +160,12 @@ extern "C" int nib_visual_merge(int dtype, const void* token_embeddings, int64_t
   if (tokens > 0) {
     int64_t b = (tokens + 255) / 256;
     if (b > kMaxGrid) b = kMaxGrid;
-    visual_row_map_fill<<<static_cast<unsigned>(b), 256, 0, st>>>(row_map, tokens);
+    ::nib::launch_k(visual_row_map_fill, static_cast<unsigned>(b), 256, 0, st, row_map, tokens);
   }
   if (num_replacements > 0 && tokens > 0) {
     int64_t b = (num_replacements + 255) / 256;
     if (b > kMaxGrid) b = kMaxGrid;
-    visual_row_map_scatter<<<static_cast<unsigned>(b), 256, 0, st>>>(output_rows, num_replacements,
+    ::nib::launch_k(visual_row_map_scatter, static_cast<unsigned>(b), 256, 0, st, output_rows, num_replacements,
                                                                       tokens, row_map, status);
   }
   const int64_t R = num_layers > 0 ? num_replacements : 0;  // DeepStack warps only with layers
@@ -170,7 +173,7 @@ extern "C" int nib_visual_merge(int dtype, const void* token_embeddings, int64_t
   if (warps > 0) {
     int64_t b = (warps + 7) / 8;  // one warp per output row, one-shot grid
     if (b > kMaxGrid) b = kMaxGrid;
-    visual_merge_kernel<<<static_cast<unsigned>(b), 256, 0, st>>>(
+    ::nib::launch_k(visual_merge_kernel, static_cast<unsigned>(b), 256, 0, st,
         static_cast<const char*>(token_embeddings), token_row_stride * elem_size(dtype), tokens,
         hidden, dtype, sources, num_sources, num_layers, source_index, feature_rows, R, row_map,
         static_cast<char*>(merged), static_cast<char*>(deepstack_out), status);

@@ -112,13 +112,15 @@ def _rope_args(rotary_emb):
 def attention_prologue(qkv: torch.Tensor, *, num_heads: int, num_kv_heads: int, head_dim: int,
                        positions: torch.Tensor, rotary_emb, q_norm=None, k_norm=None,
                        k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,
-                       slot_mapping: torch.Tensor | None = None):
+                       slot_mapping: torch.Tensor | None = None, emit_k: bool = True):
     """Fused q/k norm + rotary + paged store -> ``(q, k, v)``.
 
     ``q_norm``/``k_norm`` are RMSNorm-like modules (``weight``, ``eps``) or
     ``None``; ``rotary_emb`` is a ``RotaryEmbedding`` (table) or a
     ``MultimodalRotaryEmbedding``. The store runs when both caches are
     non-empty, as in ``Attention.forward`` (``attention.py:87-93``).
+    ``emit_k=False`` with a store: rotated k goes to the key cache only and
+    the returned ``k`` is ``None`` (for attention that reads the cache).
     """
     q_size, kv_size = num_heads * head_dim, num_kv_heads * head_dim
     q, k, v = qkv.split([q_size, kv_size, kv_size], dim=-1)
@@ -130,6 +132,7 @@ def attention_prologue(qkv: torch.Tensor, *, num_heads: int, num_kv_heads: int, 
         validate_store_inputs(k, v, k_cache, v_cache, slot_mapping)
     if (q_norm is None) != (k_norm is None):
         raise ValueError("q_norm and k_norm must be given together")
+    emit_k = emit_k or not store
     if not ops.prologue_supported(q, k, v if store else None):
         # unusual head size / layout: the same stages as separate kernels
         if q_norm is not None:
@@ -146,7 +149,8 @@ def attention_prologue(qkv: torch.Tensor, *, num_heads: int, num_kv_heads: int, 
     cache = {}
     if store:
         cache = dict(v=v, key_cache=k_cache, value_cache=v_cache, slot_mapping=slot_mapping)
-    q_rot, k_rot = ops.qk_prologue(q, k, positions=positions, **norm, **_rope_args(rotary_emb), **cache)
+    q_rot, k_rot = ops.qk_prologue(q, k, positions=positions, **norm, **_rope_args(rotary_emb), **cache,
+                                   emit_k=emit_k)
     return q_rot, k_rot, v
 
 

@@ -50,8 +50,12 @@ def _prologue_then_attend(self, qkv: torch.Tensor, positions: torch.Tensor, q_no
                  positions=positions, rotary_emb=self.rotary_emb, q_norm=q_norm, k_norm=k_norm)
     stored = getattr(attn, "forward_stored", None)
     if stored is not None and k_cache.numel() and v_cache.numel():
+        ctx = _step_context()
+        # only prefill without a block table reads this step's k directly; decode
+        # and prefix-cached / chunked prefill read k from the cache
+        emit_k = bool(ctx.is_prefill and ctx.block_tables is None)
         q, k, v = attention_prologue(qkv, k_cache=k_cache, v_cache=v_cache,
-                                     slot_mapping=_step_context().slot_mapping, **shape)
+                                     slot_mapping=ctx.slot_mapping, emit_k=emit_k, **shape)
         return stored(q, k, v)
     q, k, v = attention_prologue(qkv, **shape)
     return attn(q, k, v)

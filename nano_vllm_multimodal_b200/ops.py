@@ -123,18 +123,22 @@ def prologue_supported(*tensors) -> bool:
 
 def qk_prologue(q, k, *, v=None, positions=None, q_weight=None, k_weight=None, eps=1e-6,
                 rope_mode=ROPE_NONE, cos_sin_cache=None, inv_freq=None, sections=(),
-                key_cache=None, value_cache=None, slot_mapping=None, variant=0):
+                key_cache=None, value_cache=None, slot_mapping=None, variant=0, emit_k=True):
     """Per-head norm + RoPE/M-RoPE + paged store in one kernel -> ``(q_rot, k_rot)``.
 
     ``variant``: 0 picks automatically, 1 forces the register-staged kernel,
     2 the bulk-copy pipelined kernel (q/k/v consecutive ranges of one row).
-    Both give bit-identical results."""
+    Both give bit-identical results.
+
+    ``emit_k=False`` (only with the caches): rotated k is written to the key
+    cache alone and ``k_rot`` is ``None``; decode and prefill over a block
+    table read k from the cache, so the contiguous copy would go unread."""
     st = _status_for(q)
-    out = _ops().qk_prologue(q, k, v, positions, q_weight, k_weight, float(eps), int(rope_mode),
-                             cos_sin_cache, inv_freq, list(sections), key_cache, value_cache,
-                             slot_mapping, st, int(variant))
+    q_rot, k_rot = _ops().qk_prologue(q, k, v, positions, q_weight, k_weight, float(eps), int(rope_mode),
+                                      cos_sin_cache, inv_freq, list(sections), key_cache, value_cache,
+                                      slot_mapping, st, int(variant), bool(emit_k))
     _check_status(st, "qk_prologue")
-    return out
+    return q_rot, (k_rot if emit_k else None)
 
 
 def rope(positions, q, k, cos_sin_cache):

@@ -97,8 +97,10 @@ def _cpu_stand_ins():
 
     def qk_prologue(q, k, *, v=None, positions=None, q_weight=None, k_weight=None, eps=1e-6,
                     rope_mode=0, cos_sin_cache=None, inv_freq=None, sections=(), key_cache=None,
-                    value_cache=None, slot_mapping=None, variant=0):
+                    value_cache=None, slot_mapping=None, variant=0, emit_k=True):
         CALLS["qk_prologue.store" if key_cache is not None else "qk_prologue.nostore"] += 1
+        if not emit_k:
+            CALLS["qk_prologue.cache_only_k"] += 1
         if q_weight is not None:
             q, k = o.rms_norm(q, q_weight, eps), o.rms_norm(k, k_weight, eps)
         if rope_mode == ops.ROPE_TABLE:
@@ -108,7 +110,7 @@ def _cpu_stand_ins():
             q, k = o.mrope_forward(positions, q, k, inv_freq, tuple(sections), strategy)
         if key_cache is not None:
             o.paged_store_(k, v, key_cache, value_cache, slot_mapping)
-        return q, k
+        return q, (k if emit_k else None)
 
     def embedding(ids, weight, vocab_start=0, vocab_end=None, mask=False):
         return o.embedding(ids - vocab_start, weight)

@@ -83,6 +83,8 @@ def test_fused_route_through_reference_models_cpu(tmp_path):
     assert "qk_prologue.nostore" not in fused_calls and "paged_store" not in fused_calls
     assert fused_calls.get("add_rms_norm_deepstack") == 3 and "deepstack_add" not in fused_calls
     assert fused_calls.get("deepstack_row_index") == 1
+    # decode steps read k from the cache: no contiguous rotated k is written
+    assert fused_calls.get("qk_prologue.cache_only_k") == ATTENTION_LAYERS
     # the per-op route: rotary without the store (the reference's attention stores), three DeepStack adds
     assert perop_calls.get("qk_prologue.nostore") == ATTENTION_LAYERS * STEPS
     assert "qk_prologue.store" not in perop_calls and perop_calls.get("deepstack_add") == 3

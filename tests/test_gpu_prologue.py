@@ -283,3 +283,44 @@ def test_pipelined_variant_rejects_split_layouts():
         ops.qk_prologue(q, k, rope_mode=ops.ROPE_NONE, variant=2)
     aq, ak = ops.qk_prologue(q, k, rope_mode=ops.ROPE_NONE, variant=0)  # auto: register kernel
     assert torch.equal(aq, q) and torch.equal(ak, k)
+
+
+@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("config,tokens,rope_kind", [(2, 256, "table"), (3, 4096, "interleaved"),
+                                                     (4, 2048, "chunked")])
+def test_cache_only_k_matches_the_full_prologue(variant, config, tokens, rope_kind):
+    """``emit_k=False`` (decode / chunked prefill, which read k from the cache):
+    the same rotated q and the same cache bytes as with the contiguous k written,
+    in both kernel variants; no k comes back."""
+    d = W.make_layer_inputs(config, tokens=tokens)
+    shp = d["shape"]
+    nq, nkv = shp.num_heads, shp.num_kv_heads
+    qkv = d["qkv"].cuda()
+    q, k, v = qkv.split([nq * 128, nkv * 128, nkv * 128], -1)
+    q, k, v = q.view(-1, nq, 128), k.view(-1, nkv, 128), v.view(-1, nkv, 128)
+    if rope_kind == "table":
+        rope = dict(rope_mode=ops.ROPE_TABLE,
+                    cos_sin_cache=O.rope_cos_sin_cache(128, shp.max_position, shp.theta).cuda())
+    else:
+        mode = ops.ROPE_MROPE_INTERLEAVED if rope_kind == "interleaved" else ops.ROPE_MROPE_CHUNKED
+        rope = dict(rope_mode=mode, inv_freq=O.mrope_inv_freq(128, shp.theta).cuda(), sections=shp.sections)
+    norm = dict(q_weight=d["q_weight"].cuda(), k_weight=d["k_weight"].cuda(), eps=1e-6) if shp.qk_norm else {}
+    outs = []
+    for emit_k in (True, False):
+        kc, vc = d["key_cache"].cuda(), d["value_cache"].cuda()
+        q_rot, k_rot = ops.qk_prologue(q, k, v=v, positions=d["positions"].cuda(), **norm, **rope,
+                                       key_cache=kc, value_cache=vc, slot_mapping=d["slot_mapping"].cuda(),
+                                       variant=variant, emit_k=emit_k)
+        outs.append((q_rot, k_rot, kc, vc))
+    (q1, k1, kc1, vc1), (q2, k2, kc2, vc2) = outs
+    assert k2 is None and k1 is not None
+    assert_bitexact(q2, q1.cpu(), "q")
+    assert_bitexact(kc2, kc1.cpu(), "key cache")
+    assert_bitexact(vc2, vc1.cpu(), "value cache")
+
+
+def test_cache_only_k_needs_the_caches():
+    q = torch.zeros(4, 2, 128, dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros(4, 1, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError, match="emit_k=False needs the caches"):
+        ops.qk_prologue(q, k, emit_k=False)
