@@ -150,7 +150,7 @@ def positions_for(config: int, shape: Shape, seeds, tokens: int):
     if config == 4:
         chunk, _ = image_positions([("text", 1024), ("image", 1, 32, 64), ("text", 2048),
                                     ("image", 1, 32, 64), ("text", 1024)])
-        dec = torch.randint(0, 16384, (120,), generator=seeds(), device="cpu")
+        dec = torch.randint(0, 16384, (120,), generator=seeds(), device=seeds.device).cpu()
         pos = torch.cat((chunk, dec.expand(3, -1)), dim=1)
         return pos[:, :tokens].contiguous().to(seeds.device)
     if config == 5:

@@ -12,6 +12,12 @@ Usage: ``python tests/_model_step.py REF_DIR DEVICE MODE OUT.pt``
   * ``fused``: after ``install()``, where the model classes' forwards run the
     fused prologue (q/k norm, rotary and K/V store in one launch) and fold the
     Qwen3-VL residual adds and DeepStack rows into the norms
+  * ``truth``: the reference's model in float64 (the same bf16 weights and
+    inputs, widened; its norms compute in float32), attention as float64
+    SDPA: the yardstick both bf16 runs are measured against. (Not float32:
+    there the reference's ``RMSNorm.add_rms_forward`` would update its input
+    in place, since ``x.float()`` returns ``x`` itself, and the residual
+    would alias the normalised output.)
 
 On ``cpu`` the package's ops are replaced by CPU stand-ins computed with the
 oracle in the reference's own rounding order. That makes the fused and per-op
@@ -57,11 +63,12 @@ from nanovllm.utils.context import reset_context, set_context  # noqa: E402
 
 CALLS: Counter = Counter()
 
-if MODE != "reference":
+if MODE not in ("reference", "truth"):
     from nano_vllm_multimodal_b200.integration import install
     install(fused=(MODE == "fused"))
 
 BF16 = torch.bfloat16
+DT = torch.float64 if MODE == "truth" else BF16  # the models' compute dtype
 HIDDEN, HEADS, KV_HEADS, HEAD_DIM, INTER, VOCAB = 512, 4, 2, 128, 1024, 128
 BLOCKS, BLOCK_SIZE = 4, 256
 
@@ -136,6 +143,7 @@ def _sdpa_varlen(q, k, v, *, max_seqlen_q, cu_seqlens_q, max_seqlen_k, cu_seqlen
     assert block_table is None and causal
     CALLS["attention.prefill"] += 1
     out = torch.empty_like(q)
+    dev = q.device
     group = q.shape[1] // k.shape[1]
     for i in range(cu_seqlens_q.numel() - 1):
         qs, qe = int(cu_seqlens_q[i]), int(cu_seqlens_q[i + 1])
@@ -144,7 +152,7 @@ def _sdpa_varlen(q, k, v, *, max_seqlen_q, cu_seqlens_q, max_seqlen_k, cu_seqlen
         ki = k[ks:ke].double().repeat_interleave(group, dim=1).transpose(0, 1)
         vi = v[ks:ke].double().repeat_interleave(group, dim=1).transpose(0, 1)
         s = qi @ ki.transpose(1, 2) * softmax_scale
-        mask = torch.ones(qe - qs, ke - ks, dtype=torch.bool).tril(diagonal=(ke - ks) - (qe - qs))
+        mask = torch.ones(qe - qs, ke - ks, dtype=torch.bool, device=dev).tril(diagonal=(ke - ks) - (qe - qs))
         s = s.masked_fill(~mask, float("-inf"))
         out[qs:qe] = (torch.softmax(s, dim=-1) @ vi).transpose(0, 1).to(q.dtype)
     return out
@@ -158,11 +166,31 @@ def _decode_attention(q, k_cache, v_cache, *, cache_seqlens, block_table, softma
                                     softmax_scale).unsqueeze(1)
 
 
+def _decode_attention_device(q, k_cache, v_cache, *, cache_seqlens, block_table, softmax_scale, causal):
+    """Paged decode in float64 with torch ops on q's device (the ``truth`` run)."""
+    CALLS["attention.decode"] += 1
+    bs = k_cache.shape[1]
+    group = q.shape[2] // k_cache.shape[2]
+    out = torch.zeros_like(q)
+    for b in range(q.shape[0]):
+        n = int(cache_seqlens[b])
+        t = torch.arange(n, device=q.device)
+        slots = block_table[b].long()[t // bs] * bs + t % bs
+        k = k_cache.flatten(0, 1)[slots].double().repeat_interleave(group, dim=1)  # [n, heads, D]
+        v = v_cache.flatten(0, 1)[slots].double().repeat_interleave(group, dim=1)
+        s = torch.einsum("hd,nhd->hn", q[b, 0].double(), k) * softmax_scale
+        out[b, 0] = torch.einsum("hn,nhd->hd", torch.softmax(s, dim=-1), v).to(q.dtype)
+    return out
+
+
 if DEVICE == "cpu":
-    if MODE != "reference":
+    if MODE not in ("reference", "truth"):
         _cpu_stand_ins()
     ref_attention.flash_attn_varlen_func = _sdpa_varlen
     ref_attention.flash_attn_with_kvcache = _decode_attention
+elif MODE == "truth":
+    ref_attention.flash_attn_varlen_func = _sdpa_varlen
+    ref_attention.flash_attn_with_kvcache = _decode_attention_device
 
 
 # ----------------------------------------------------------------------------- models
@@ -188,8 +216,9 @@ def _configs():
 
 
 def _seeded(shape, seed, *, mean=0.0, std=1.0, dtype=BF16):
+    """bf16 values (widened to ``dtype`` in the float32 run, so every run sees the same numbers)."""
     g = torch.Generator().manual_seed(seed)
-    return (torch.randn(shape, generator=g) * std + mean).to(dtype)
+    return (torch.randn(shape, generator=g) * std + mean).to(BF16).to(dtype)
 
 
 def _init_weights(model):
@@ -213,7 +242,7 @@ def _attach_caches(model, device):
     backend = PyTorchPagedKVBackend()
     for module in model.modules():
         if hasattr(module, "k_cache") and hasattr(module, "v_cache"):
-            k = torch.full((BLOCKS, BLOCK_SIZE, KV_HEADS, HEAD_DIM), -3.0, dtype=BF16, device=device)
+            k = torch.full((BLOCKS, BLOCK_SIZE, KV_HEADS, HEAD_DIM), -3.0, dtype=DT, device=device)
             v = torch.full_like(k, -3.0)
             module.k_cache, module.v_cache = k, v
             if hasattr(module, "paged_kv_backend"):
@@ -234,7 +263,7 @@ def _record_layers(model, sink):
 
 def _run(name, build, axes, device):
     torch.manual_seed(0)
-    torch.set_default_dtype(BF16)
+    torch.set_default_dtype(DT)
     torch.set_default_device(device)
     try:
         model = build()
@@ -268,8 +297,8 @@ def _run(name, build, axes, device):
     if name == "qwen3_vl":
         rows = torch.arange(lens[0] + 4, lens[0] + 10, dtype=torch.long)
         kwargs = dict(visual_token_rows=rows.to(device),
-                      deepstack_visual_embeds=tuple(_seeded((rows.numel(), HIDDEN), seed + 1 + j).to(device)
-                                                    for j in range(3)))
+                      deepstack_visual_embeds=tuple(_seeded((rows.numel(), HIDDEN), seed + 1 + j,
+                                                            dtype=DT).to(device) for j in range(3)))
     layer_out = []
     hooks = _record_layers(model, layer_out)
     with torch.inference_mode():

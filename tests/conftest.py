@@ -17,3 +17,16 @@ def pytest_configure(config):
 def golden():
     import torch
     return torch.load(ROOT / "tests" / "golden" / "golden.pt", weights_only=True)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """Write the measured parity exceptions (tests/_util.PARITY_REPORT) to
+    gpurun_out/parity_report.json when a GPU session produced any."""
+    try:
+        from tests._util import PARITY_REPORT
+    except ImportError:
+        return
+    out = ROOT / "gpurun_out"
+    if PARITY_REPORT and out.is_dir():
+        import json
+        (out / "parity_report.json").write_text(json.dumps(PARITY_REPORT, indent=1, sort_keys=True))

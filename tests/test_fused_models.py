@@ -90,10 +90,8 @@ def test_fused_route_through_reference_models_cpu(tmp_path):
     assert "qk_prologue.store" not in perop_calls and perop_calls.get("deepstack_add") == 3
 
 
-def _ulp_bf16(x):
-    """One bf16 ulp at the magnitude of each element (the spacing at |x|)."""
-    mag = x.abs().clamp_min(2.0 ** -126)
-    return torch.exp2(torch.floor(torch.log2(mag)) - 7)
+def _rel(x, t):
+    return float((x.double() - t.double()).norm() / t.double().norm().clamp_min(1e-30))
 
 
 @need_ref
@@ -104,25 +102,25 @@ def test_fused_route_through_reference_models_gpu(tmp_path):
     * the fused route equals the per-op route bit for bit: every layer output,
       both steps' final hidden states and every K/V cache (both routes use the
       same kernels; fusing changes nothing in the arithmetic);
-    * against the reference's own eager GPU run (torch CUDA reductions, its
-      store, flash-attn's decode) every tensor agrees within the bound below.
-      Per op the kernels are within 1-2 bf16 ulp of the reference; through
-      three layers of GEMMs those last-bit differences spread, so the bound
-      is stated on the whole model: at most 1% of elements beyond 2 ulp, none
-      beyond 2**-4 * max(1, |ref|), and the relative L2 error under 2**-8."""
-    runs = _run_modes("cuda", tmp_path)
-    fused, perop, ref = runs["fused"][1], runs["perop"][1], runs["reference"][1]
+    * the fused route is as accurate as the reference's own bf16 run on the
+      GPU (eager: torch CUDA reductions, two-rounding SiluAndMul, its store,
+      flash-attn's decode). Both are measured against the same model in
+      float64 (``truth``: the same bf16 weights and inputs widened, attention
+      as float64 SDPA). For every tensor the fused route's relative L2 error
+      is at most 1.25x the reference's own plus 2**-12. The two bf16 runs are
+      not compared element by element: each op's last-bit differences (1-2
+      ulp, bounded op by op in the other tests) spread through the GEMMs."""
+    runs = _run_modes("cuda", tmp_path, ("reference", "perop", "fused", "truth"))
+    fused, perop, ref, truth = (runs[m][1] for m in ("fused", "perop", "reference", "truth"))
     for name, x, y in _pairs(fused, perop):
         assert torch.equal(x, y), f"fused vs per-op {name}: max diff {(x - y).abs().max().item()}"
     report = {}
+    truth_of = {name: t for name, _, t in _pairs(fused, truth)}
     for name, x, y in _pairs(fused, ref):
-        d = (x - y).abs()
-        over2 = (d > 2 * _ulp_bf16(y)).float().mean().item()
-        rel = (d.norm() / y.norm().clamp_min(1e-30)).item()
-        report[name] = dict(max=d.max().item(), frac_over_2ulp=over2, rel_l2=rel)
-        assert over2 <= 0.01, (name, report[name])
-        assert bool((d <= 2.0 ** -4 * y.abs().clamp_min(1.0)).all()), (name, report[name])
-        assert rel < 2.0 ** -8, (name, report[name])
+        t = truth_of[name]
+        e_fused, e_ref = _rel(x, t), _rel(y, t)
+        report[name] = dict(fused_rel_err=e_fused, reference_rel_err=e_ref)
+        assert e_fused <= 1.25 * e_ref + 2.0 ** -12, (name, report[name])
     out = ROOT / "gpurun_out"
     if out.is_dir():
         (out / "fused_models_vs_reference.json").write_text(json.dumps(report, indent=1))

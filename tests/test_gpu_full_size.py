@@ -6,7 +6,9 @@ through properties that do not depend on size, checked on the device:
 * every written slot holds exactly the token's rotated k and raw v, and every
   other slot keeps its sentinel (-3);
 * a random sample of tokens / rows matches the CPU oracle bit for bit (norms in
-  the kernels' summation order, M-RoPE given the kernel's own cos/sin) and
+  the kernels' summation order, M-RoPE given the kernel's own cos/sin), and
+  against the oracle's own cos/sin within 1 ulp except where a cos/sin value
+  differs from the host's, there within that difference's propagated bound;
   SiluAndMul within 1 ulp of the fp32 single-rounding result;
 * the many-sequence paged gather over the full cache equals direct indexing.
 
@@ -18,7 +20,7 @@ import torch
 
 import oracle as O
 from nano_vllm_multimodal_b200 import ops, workloads as W
-from tests._util import assert_bitexact, assert_ulp
+from tests._util import assert_bitexact, assert_trig_bounded, assert_ulp
 
 pytestmark = pytest.mark.gpu
 
@@ -100,6 +102,17 @@ def test_c5_full_prologue_variants_placement_and_sample(c5):
     eq, ek = O.apply_mrope(qs, ks, cos.cpu(), sin.cpu(), SHP.sections, "interleaved")
     assert_bitexact(q1[idx], eq, "q sample")
     assert_bitexact(k1[idx], ek, "k sample")
+    # the same sample end to end against the oracle's own cos/sin (host libm):
+    # cos/sin within 1 ulp, rarely different, and the rotation within the
+    # propagated bound of such a difference
+    cc, cs = O.mrope_cos_sin(c5["positions"][:, idx].cpu(), c5["inv_freq"].cpu(), torch.bfloat16)
+    dc = assert_ulp(cos, cc, 1, "C5 sample cos vs CPU")
+    ds = assert_ulp(sin, cs, 1, "C5 sample sin vs CPU")
+    assert float(((dc > 0) | (ds > 0)).float().mean()) < 1e-3, "C5 sample: too many cos/sin differ from the CPU"
+    trig_differs = ((dc > 0) | (ds > 0)).any(dim=0).any(dim=-1)
+    oq, ok = O.apply_mrope(qs, ks, cc, cs, SHP.sections, "interleaved")
+    assert_trig_bounded(q1[idx], oq, qs, trig_differs, "C5 full-size prologue q, oracle cos/sin")
+    assert_trig_bounded(k1[idx], ok, ks, trig_differs, "C5 full-size prologue k, oracle cos/sin")
 
     # the many-sequence gather over the full cache: 8 sequences x 16,384 tokens
     seqs, n = 8, SHP.extra["gather_len"]
