@@ -698,47 +698,56 @@ def step_inputs_component(out, device):
 
 
 def decode_attention_component(out, record, flush, device, requests=256):
-    """Paged decode attention at C2 decode: 256 requests, 16/8 heads of 128, 256-token
-    blocks, contexts U[1, 8192] (C2 positions U[0, 8191] plus the new token); the kernel
-    against the roofline, and flash-attn's own flash_attn_with_kvcache (the reference's
-    decode kernel) on the same inputs when it runs on this GPU."""
+    """Paged decode attention at C2 decode: 256 requests, 256-token blocks, contexts
+    U[1, 8192] (C2 positions U[0, 8191] plus the new token), at two head layouts:
+    16/8 heads of 128 (Qwen3, GQA 2) and 16/2 (Qwen2.5-VL, GQA 8: four times the
+    q.K and P.V work per cached byte). Each kernel against the roofline (the
+    tensor-core kernel, the default, and the CUDA-core one), and flash-attn's own
+    flash_attn_with_kvcache (the reference's decode kernel) on the same inputs."""
     from nano_vllm_multimodal_b200 import ops
 
-    g = torch.Generator().manual_seed(5151)
-    B, NQ_, NKV_, D_, BS_ = requests, 16, 8, 128, 256
-    lens = torch.randint(1, 8193, (B,), generator=g, dtype=torch.int32)
-    need = (lens + BS_ - 1) // BS_
-    nblocks = int(need.sum()) + 16
-    width = int(need.max())
-    perm = torch.randperm(nblocks, generator=g).to(torch.int32)
-    tables = torch.full((B, width), 0, dtype=torch.int32)
-    at = 0
-    for b in range(B):
-        n = int(need[b])
-        tables[b, :n] = perm[at:at + n]
-        at += n
-    kc = torch.randn(nblocks, BS_, NKV_, D_, device=device, dtype=torch.bfloat16)
-    vc = torch.randn(nblocks, BS_, NKV_, D_, device=device, dtype=torch.bfloat16)
-    q = torch.randn(B, NQ_, D_, device=device, dtype=torch.bfloat16)
-    cl, tb = lens.to(device), tables.to(device)
-    scale = D_ ** -0.5
-    ms = _time_op(flush=flush, fn=lambda: ops.decode_attention(q, kc, vc, cl, tb, scale, 8192))
-    nbytes = int(lens.sum()) * NKV_ * D_ * 2 * 2 + B * NQ_ * D_ * 2 * 2 + B * 4 + int(need.sum()) * 4
-    record("decode_attention", ms, nbytes,
-           f"C2 decode: {B} requests, 16/8 heads x 128, 256-token blocks, contexts U[1,8192]")
-    try:
-        from flash_attn import flash_attn_with_kvcache as fa
-
-        ref = fa(q.unsqueeze(1), kc, vc, cache_seqlens=cl, block_table=tb, softmax_scale=scale, causal=True)
+    for name, NQ_, NKV_ in (("decode_attention", 16, 8), ("decode_attention_gqa8", 16, 2)):
+        g = torch.Generator().manual_seed(5151)
+        B, D_, BS_ = requests, 128, 256
+        lens = torch.randint(1, 8193, (B,), generator=g, dtype=torch.int32)
+        need = (lens + BS_ - 1) // BS_
+        nblocks = int(need.sum()) + 16
+        width = int(need.max())
+        perm = torch.randperm(nblocks, generator=g).to(torch.int32)
+        tables = torch.full((B, width), 0, dtype=torch.int32)
+        at = 0
+        for b in range(B):
+            n = int(need[b])
+            tables[b, :n] = perm[at:at + n]
+            at += n
+        kc = torch.randn(nblocks, BS_, NKV_, D_, device=device, dtype=torch.bfloat16)
+        vc = torch.randn(nblocks, BS_, NKV_, D_, device=device, dtype=torch.bfloat16)
+        q = torch.randn(B, NQ_, D_, device=device, dtype=torch.bfloat16)
+        cl, tb = lens.to(device), tables.to(device)
+        scale = D_ ** -0.5
+        nbytes = int(lens.sum()) * NKV_ * D_ * 2 * 2 + B * NQ_ * D_ * 2 * 2 + B * 4 + int(need.sum()) * 4
+        cfg = (f"C2 decode: {B} requests, {NQ_}/{NKV_} heads x 128 (GQA {NQ_ // NKV_}), 256-token blocks, "
+               "contexts U[1,8192]; tensor-core kernel")
+        ms = _time_op(flush=flush, fn=lambda: ops.decode_attention(q, kc, vc, cl, tb, scale, 8192))
+        record(name, ms, nbytes, cfg)
         mine = ops.decode_attention(q, kc, vc, cl, tb, scale, 8192)
-        diff = float((ref[:, 0].float() - mine.float()).abs().max())
-        ms_fa = _time_op(flush=flush, fn=lambda: fa(q.unsqueeze(1), kc, vc, cache_seqlens=cl, block_table=tb,
-                                                    softmax_scale=scale, causal=True))
-        out["decode_attention"]["flash_attn_ms"] = round(ms_fa, 4)
-        out["decode_attention"]["max_abs_diff_vs_flash_attn"] = round(diff, 5)
-    except Exception as e:  # the library may carry no kernels for this GPU
-        out["decode_attention"]["flash_attn"] = f"unavailable: {type(e).__name__}: {str(e)[:120]}"
-    del kc, vc
+        ms_fma = _time_op(flush=flush, fn=lambda: ops.decode_attention(q, kc, vc, cl, tb, scale, 8192,
+                                                                       variant=ops.DECODE_CUDA_CORES))
+        out[name]["cuda_core_kernel_ms"] = round(ms_fma, 4)
+        out[name]["cuda_core_kernel_frac"] = round(nbytes / (ms_fma / 1000.0) / 1e9 / measured_hbm_peak(), 4)
+        try:
+            from flash_attn import flash_attn_with_kvcache as fa
+
+            ref = fa(q.unsqueeze(1), kc, vc, cache_seqlens=cl, block_table=tb, softmax_scale=scale, causal=True)
+            diff = float((ref[:, 0].float() - mine.float()).abs().max())
+            ms_fa = _time_op(flush=flush, fn=lambda: fa(q.unsqueeze(1), kc, vc, cache_seqlens=cl, block_table=tb,
+                                                        softmax_scale=scale, causal=True))
+            out[name]["flash_attn_ms"] = round(ms_fa, 4)
+            out[name]["flash_attn_frac"] = round(nbytes / (ms_fa / 1000.0) / 1e9 / measured_hbm_peak(), 4)
+            out[name]["max_abs_diff_vs_flash_attn"] = round(diff, 5)
+        except Exception as e:  # the library may carry no kernels for this GPU
+            out[name]["flash_attn"] = f"unavailable: {type(e).__name__}: {str(e)[:120]}"
+        del kc, vc
 
 
 def rows_flushed_rounds(flush, device, rounds=3):

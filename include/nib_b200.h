@@ -158,7 +158,10 @@ typedef struct nib_decode_attention_args {
   int32_t struct_size; /* sizeof(nib_decode_attention_args) */
   int32_t dtype;
   int64_t batch;
-  int32_t num_heads, num_kv_heads, head_dim, reserved;
+  int32_t num_heads, num_kv_heads, head_dim;
+  int32_t variant;     /* 0: tensor-core kernel where it applies (bf16/f16, head_dim 64/128,
+                          <= 16 q heads per kv head, block_size % 16 == 0), else the CUDA-core
+                          kernel; 1: CUDA-core kernel; 2: tensor-core kernel or NIB_ERR_UNSUPPORTED */
   const void* q;
   int64_t q_batch_stride, q_head_stride;
   const void* key_cache;

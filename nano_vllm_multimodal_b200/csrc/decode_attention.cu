@@ -7,8 +7,10 @@
 // scale) V over the request's first context_lens[b] cached tokens, grouped-query
 // heads sharing kv head h / (num_heads / num_kv_heads).
 //
-// HBM-bound (about 2 flops per cached byte), so the arithmetic runs on the CUDA
-// cores in fp32 and the design is about bytes in flight:
+// This file is the CUDA-core kernel: bf16/f16 at any head_dim the ABI takes,
+// and every layout the tensor-core kernel (decode_attention_mma.cu, the
+// default where it applies) does not take. Its arithmetic runs in fp32 and the
+// design is about bytes in flight:
 //   * a CTA owns (request, kv head, split of the context); its warps split
 //     the q heads of that kv head (two per warp) and the tokens;
 //   * a token's 16-byte K and V vectors are spread over D/8 lanes, so one warp
@@ -24,6 +26,11 @@
 #include "dispatch.cuh"
 
 namespace nib {
+
+// the tensor-core kernel (decode_attention_mma.cu)
+bool decode_mma_eligible(const nib_decode_attention_args& a);
+size_t decode_mma_smem(int head_dim);
+int launch_decode_mma(const nib_decode_attention_args& a, int splits, cudaStream_t st);
 
 constexpr int kDecodeWarps = 8;
 constexpr int kDecodeUnroll = 2;           // token steps per stage
@@ -479,6 +486,20 @@ static int launch_decode(const nib_decode_attention_args& a, const DecodePlan& p
   return launch_status("decode_attention");
 }
 
+// the split partials' combine after the tensor-core kernel (same workspace format)
+template <typename T, int D>
+static int launch_combine(const nib_decode_attention_args& a, int splits, cudaStream_t st) {
+  DecodeParams p{};
+  p.out = a.out;
+  p.o_bs = a.out_batch_stride;
+  p.o_hs = a.out_head_stride;
+  p.ws = static_cast<float*>(a.workspace);
+  p.num_heads = a.num_heads;
+  p.splits = splits;
+  ::nib::launch_k(decode_combine_kernel<T, D>, static_cast<unsigned>(a.batch * a.num_heads), D, 0, st, p);
+  return launch_status("decode_attention (combine)");
+}
+
 template <typename T, int D>
 static int launch_decode_d(const nib_decode_attention_args& a, const DecodePlan& pl, cudaStream_t st) {
   return pl.hpw == 2 ? launch_decode<T, D, 2>(a, pl, st) : launch_decode<T, D, 1>(a, pl, st);
@@ -516,6 +537,17 @@ extern "C" int nib_decode_attention(const nib_decode_attention_args* a, void* st
   NIB_REQUIRE(need == 0 || (a->workspace && a->workspace_bytes >= need && aligned16(a->workspace)),
               "decode_attention: workspace of %lld bytes needed", static_cast<long long>(need));
   const cudaStream_t st = as_stream(stream);
+  NIB_REQUIRE(a->variant >= 0 && a->variant <= 2, "decode_attention: bad variant %d", a->variant);
+  if (a->variant != 1 && decode_mma_eligible(*a)) {
+    const int rc = launch_decode_mma(*a, pl.splits, st);
+    if (rc != NIB_OK || pl.splits == 1) return rc;
+    if (a->dtype == NIB_BF16)
+      return a->head_dim == 64 ? launch_combine<__nv_bfloat16, 64>(*a, pl.splits, st)
+                               : launch_combine<__nv_bfloat16, 128>(*a, pl.splits, st);
+    return a->head_dim == 64 ? launch_combine<__half, 64>(*a, pl.splits, st) : launch_combine<__half, 128>(*a, pl.splits, st);
+  }
+  NIB_SUPPORT(a->variant != 2, "decode_attention: the tensor-core kernel needs bf16/f16, head_dim 64 or 128, "
+              "at most 16 q heads per kv head, a block size that is a multiple of 16 and 16-byte aligned strides");
   if (pl.smem > 200 * 1024) {
     set_error("decode_attention: shared-memory ring too large");
     return NIB_ERR_UNSUPPORTED;

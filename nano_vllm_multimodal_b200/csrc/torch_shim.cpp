@@ -418,7 +418,7 @@ void deepstack_add_(Tensor hidden, const Tensor& rows, const Tensor& vis, const 
 
 Tensor decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache,
                         const Tensor& context_lens, const Tensor& block_tables, double scale,
-                        int64_t max_context_len, const optional<Tensor>& status) {
+                        int64_t max_context_len, const optional<Tensor>& status, int64_t variant) {
   TORCH_CHECK(q.dim() == 3 && q.stride(2) == 1, "decode_attention: q must be [batch, heads, head_dim]");
   TORCH_CHECK(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes() && k_cache.stride(3) == 1 &&
                   v_cache.strides() == k_cache.strides(),
@@ -465,6 +465,7 @@ Tensor decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_
   a.out_batch_stride = out.stride(0);
   a.out_head_stride = out.stride(1);
   a.max_context_len = max_context_len;
+  a.variant = static_cast<int32_t>(variant);
   a.status = status_ptr(status);
   const int64_t need = nib_decode_attention_workspace_bytes(&a);
   TORCH_CHECK(need >= 0, "decode_attention: unsupported configuration (head_dim ", a.head_dim, ", heads ",
@@ -841,7 +842,7 @@ TORCH_LIBRARY(nanoinfer_b200, m) {
   m.def("deepstack_add(Tensor hidden, Tensor rows, Tensor vis, Tensor(a!)? status) -> Tensor");
   m.def("deepstack_row_index(Tensor rows, int tokens, Tensor(a!)? status) -> Tensor");
   m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor context_lens, Tensor block_tables, "
-        "float scale, int max_context_len, Tensor(a!)? status) -> Tensor");
+        "float scale, int max_context_len, Tensor(a!)? status, int variant=0) -> Tensor");
   m.def("visual_merge(Tensor tokens, Tensor table, int num_layers, Tensor plan, int num_replacements, "
         "Tensor(a!)? status) -> (Tensor, Tensor)");
   m.def("add_rms_norm_deepstack(Tensor x, Tensor residual, Tensor weight, float eps, Tensor vis, "

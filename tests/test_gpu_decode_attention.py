@@ -1,4 +1,5 @@
-"""Paged decode attention (``nib_decode_attention``) against the oracle and the reference.
+"""Paged decode attention (``nib_decode_attention``) against the oracle and the reference,
+both kernels: the tensor-core one (the default where it applies) and the CUDA-core one.
 
 Tolerances (attention is floating point; the kernel computes in fp32):
 * against the float64 oracle: |out - oracle| <= 2^-8 * |oracle| + 1e-4, i.e. one
@@ -58,13 +59,48 @@ def _case(seed, batch, nq, nkv, dim, bs, lens, nblocks=None, dtype=torch.bfloat1
     (8, 8, 256, 32, [0, 40, 129]),                        # MHA, head_dim 256, an empty context
 ])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_matches_oracle(nq, nkv, dim, bs, lens, dtype):
+@pytest.mark.parametrize("variant", [ops.DECODE_CUDA_CORES, ops.DECODE_TENSOR_CORES])
+def test_matches_oracle(nq, nkv, dim, bs, lens, dtype, variant):
     q, kc, vc, cl, tb = _case(nq * 1000 + dim + bs, len(lens), nq, nkv, dim, bs, lens, dtype=dtype)
     scale = dim ** -0.5
-    out = paged_decode_attention(q.cuda(), kc.cuda(), vc.cuda(), cl.cuda(), tb.cuda(), scale)
-    _close_to_oracle(out, O.paged_decode_attention(q, kc, vc, cl, tb, scale), f"{nq}/{nkv} D{dim} bs{bs}")
+    args = (q.cuda(), kc.cuda(), vc.cuda(), cl.cuda(), tb.cuda(), scale)
+    if variant == ops.DECODE_TENSOR_CORES and not _mma_shape(nq, nkv, dim, bs):
+        with pytest.raises(RuntimeError, match="tensor-core kernel needs"):
+            ops.decode_attention(*args, variant=variant)
+        return
+    out = ops.decode_attention(*args, variant=variant)
+    _close_to_oracle(out, O.paged_decode_attention(q, kc, vc, cl, tb, scale),
+                     f"{nq}/{nkv} D{dim} bs{bs} variant {variant}")
     if 0 in lens:
         assert not out[lens.index(0)].any()
+
+
+def _mma_shape(nq, nkv, dim, bs):
+    """The tensor-core kernel's shapes: head_dim 64/128, <= 16 q heads per kv head,
+    block size a multiple of 16."""
+    return dim in (64, 128) and nq // nkv <= 16 and bs % 16 == 0
+
+
+@pytest.mark.parametrize("nq,nkv", [(16, 8), (16, 2), (12, 1), (16, 16)])
+def test_tensor_cores_match_cuda_cores_and_ignore_stale_slots(nq, nkv):
+    """The tensor-core kernel against the CUDA-core kernel and the oracle, with
+    NaN in every cache slot past each context (a block's unwritten tail), a split
+    context whose split boundaries fall inside 16-token tiles, and a context of
+    one token. Stale slots must not reach the output (0 x NaN is NaN)."""
+    lens = [1, 17, 255, 4000, 16]
+    q, kc, vc, cl, tb = _case(nq * 31 + nkv, len(lens), nq, nkv, 128, 256, lens)
+    for b, n in enumerate(lens):  # poison the unwritten tail of each sequence's last block
+        last = int(tb[b, (n - 1) // 256])
+        kc[last, n % 256 or 256:] = float("nan")
+        vc[last, n % 256 or 256:] = float("nan")
+    args = (q.cuda(), kc.cuda(), vc.cuda(), cl.cuda(), tb.cuda(), 128 ** -0.5)
+    mma = ops.decode_attention(*args, variant=ops.DECODE_TENSOR_CORES)
+    fma = ops.decode_attention(*args, variant=ops.DECODE_CUDA_CORES)
+    assert not torch.isnan(mma).any() and not torch.isnan(fma).any()
+    expect = O.paged_decode_attention(q, kc, vc, cl, tb, 128 ** -0.5)
+    _close_to_oracle(mma, expect, f"tensor cores {nq}/{nkv}")
+    _close_to_oracle(fma, expect, f"CUDA cores {nq}/{nkv}")
+    assert torch.equal(ops.decode_attention(*args), mma), "the default is the tensor-core kernel"
 
 
 def test_long_contexts_split_across_ctas_and_strided_q():
@@ -75,8 +111,10 @@ def test_long_contexts_split_across_ctas_and_strided_q():
     qkv[:, :2048] = q.reshape(2, -1)
     qv = qkv.cuda()[:, :2048].view(2, 16, 128)
     assert qv.stride(0) == 32 * 128
-    out = paged_decode_attention(qv, kc.cuda(), vc.cuda(), cl.cuda(), tb.cuda(), 128 ** -0.5)
-    _close_to_oracle(out, O.paged_decode_attention(q, kc, vc, cl, tb, 128 ** -0.5), "split contexts")
+    expect = O.paged_decode_attention(q, kc, vc, cl, tb, 128 ** -0.5)
+    for variant in (ops.DECODE_CUDA_CORES, ops.DECODE_TENSOR_CORES):
+        out = ops.decode_attention(qv, kc.cuda(), vc.cuda(), cl.cuda(), tb.cuda(), 128 ** -0.5, variant=variant)
+        _close_to_oracle(out, expect, f"split contexts, variant {variant}")
 
 
 def test_flash_attn_shaped_drop_in():
@@ -93,17 +131,18 @@ def test_flash_attn_shaped_drop_in():
         flash_attn_with_kvcache(qg.unsqueeze(1), kg, vg, cache_seqlens=cg, block_table=tg, softcap=30.0)
 
 
-def test_bad_block_and_length_reported(monkeypatch):
+@pytest.mark.parametrize("variant", [ops.DECODE_CUDA_CORES, ops.DECODE_TENSOR_CORES])
+def test_bad_block_and_length_reported(monkeypatch, variant):
     monkeypatch.setenv("NANOINFER_B200_VALIDATE", "1")
     q, kc, vc, cl, tb = _case(9, 2, 16, 8, 128, 16, [20, 5])
     bad = tb.clone()
     bad[0, 1] = 999
     with pytest.raises(ValueError, match="block"):
-        ops.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), cl.cuda(), bad.cuda(), 0.1)
+        ops.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), cl.cuda(), bad.cuda(), 0.1, variant=variant)
     long = cl.clone()
     long[1] = 10_000
     with pytest.raises(ValueError, match="out of range"):
-        ops.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), long.cuda(), tb.cuda(), 0.1)
+        ops.decode_attention(q.cuda(), kc.cuda(), vc.cuda(), long.cuda(), tb.cuda(), 0.1, variant=variant)
 
 
 @pytest.mark.parametrize("batch", [4, 128])
