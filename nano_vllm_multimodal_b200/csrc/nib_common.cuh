@@ -25,13 +25,14 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // number of SMs of the current device (cached per device)
 int sm_count();
 
-// Programmatic dependent launch. Every kernel of this library is launched with
-// the programmatic-stream-serialization attribute (unless NIB_B200_PDL=0 in the
-// environment): it may be scheduled while the kernel before it on the stream
+// Programmatic dependent launch (opt-in: NIB_B200_PDL=1). Every kernel of this
+// library can be launched with the programmatic-stream-serialization
+// attribute: it may then be scheduled while the kernel before it on the stream
 // is still finishing, so its launch latency and block set-up overlap that
 // tail. Each kernel therefore starts with pdl_enter(), which waits for the
 // preceding grid to complete (and its memory to be visible) before touching
-// global memory, then lets the next kernel launch early in turn.
+// global memory, then lets the next kernel launch early in turn. Without the
+// attribute pdl_enter() returns at once.
 bool pdl_enabled();
 void note_launch_error(cudaError_t e);  // reported by the next launch_status()
 

@@ -25,6 +25,7 @@ __all__ = [
     "add_text_rms_norm_deepstack",
     "planned_visual_embeddings",
     "paged_decode_attention",
+    "paged_decode_attention_abs",
     "silu_and_mul",
     "silu_and_mul_fp32",
     "rope_cos_sin_cache",
@@ -417,6 +418,27 @@ def paged_decode_attention(q, k_cache, v_cache, context_lens, block_tables, scal
         for h in range(heads):
             p = torch.softmax((k[:, h // group] @ q[b, h].double()) * scale, dim=0)
             out[b, h] = (p @ v[:, h // group]).to(q.dtype)
+    return out
+
+
+def paged_decode_attention_abs(q, k_cache, v_cache, context_lens, block_tables, scale):
+    """The softmax-weighted mean of ``|v|`` for each output element of
+    :func:`paged_decode_attention` (float64, ``[batch, heads, head_dim]``):
+    ``sum_t p_t |v_t| / sum_t p_t``. A kernel that rounds the probabilities
+    ``p_t`` to bf16/fp16 before ``P V`` (as flash-attn's decode kernel and the
+    tensor-core kernel here do) errs by at most ``2^-8`` times this amount."""
+    batch, heads, dim = q.shape
+    group = heads // k_cache.shape[2]
+    out = torch.zeros(batch, heads, dim, dtype=torch.float64)
+    for b in range(batch):
+        n = int(context_lens[b])
+        if n == 0:
+            continue
+        k = paged_gather(k_cache, block_tables[b], n).double()
+        v = paged_gather(v_cache, block_tables[b], n).double().abs()
+        for h in range(heads):
+            p = torch.softmax((k[:, h // group] @ q[b, h].double()) * scale, dim=0)
+            out[b, h] = p @ v[:, h // group]
     return out
 
 
