@@ -390,6 +390,7 @@ decode_combine_kernel(const DecodeParams p) {
 struct DecodePlan {
   int hpw, head_groups, token_groups, warps, splits;
   size_t smem;
+  bool mma;  // the tensor-core kernel runs
 };
 
 static DecodePlan decode_plan(const nib_decode_attention_args& a) {
@@ -399,12 +400,17 @@ static DecodePlan decode_plan(const nib_decode_attention_args& a) {
   pl.head_groups = (g + pl.hpw - 1) / pl.hpw;
   pl.token_groups = pl.head_groups >= kDecodeWarps ? 1 : kDecodeWarps / pl.head_groups;
   pl.warps = pl.head_groups * pl.token_groups;
-  // splits: enough CTAs for every SM, at least 256 tokens per split
+  pl.mma = a.variant != 1 && decode_mma_eligible(a);
+  // splits: enough CTAs for every SM, at least 256 tokens per split (tensor-core
+  // kernel: at least 64, one 16-token tile per warp). The tensor-core kernel asks
+  // for 16 CTAs per SM (about 5 waves at 3 resident): at C2 decode with GQA 8
+  // (512 request x kv-head pairs, contexts U[1, 8192]) 4 gave 0.218 ms, 8 and 16
+  // 0.210 ms, 32 0.238 ms; with GQA 2 (2,048 pairs) 16 was 1.5% faster than 4.
   const int64_t ctas = a.batch * a.num_kv_heads;
-  const int64_t want = 4LL * sm_count();
+  const int64_t want = (pl.mma ? 16LL : 4LL) * sm_count();
   int64_t s = ctas >= want ? 1 : (want + ctas - 1) / ctas;
   const int64_t max_len = a.max_context_len > 0 ? a.max_context_len : a.max_blocks_per_seq * a.block_size;
-  const int64_t by_len = (max_len + 255) / 256;
+  const int64_t by_len = (max_len + (pl.mma ? 63 : 255)) / (pl.mma ? 64 : 256);
   if (kDecodeSplitTokens > 0) {
     const int64_t balance = (max_len + kDecodeSplitTokens - 1) / kDecodeSplitTokens;
     if (s < balance) s = balance;
@@ -538,7 +544,7 @@ extern "C" int nib_decode_attention(const nib_decode_attention_args* a, void* st
               "decode_attention: workspace of %lld bytes needed", static_cast<long long>(need));
   const cudaStream_t st = as_stream(stream);
   NIB_REQUIRE(a->variant >= 0 && a->variant <= 2, "decode_attention: bad variant %d", a->variant);
-  if (a->variant != 1 && decode_mma_eligible(*a)) {
+  if (pl.mma) {
     const int rc = launch_decode_mma(*a, pl.splits, st);
     if (rc != NIB_OK || pl.splits == 1) return rc;
     if (a->dtype == NIB_BF16)

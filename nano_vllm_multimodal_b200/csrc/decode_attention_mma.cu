@@ -17,7 +17,9 @@
 // with the group.
 //
 // Each warp owns every kMmaWarps-th tile of the CTA's range and a private ring
-// of kMmaStages shared-memory stages. Lane 0 loads a tile with two TMA tensor
+// of kMmaStages (2) shared-memory stages, so 3 CTAs (12 warps) fit on an SM:
+// with 3 stages and 2 CTAs per SM the GQA-8 C2 decode took 0.210 ms instead of
+// 0.203 ms. Lane 0 loads a tile with two TMA tensor
 // copies (cp.async.bulk.tensor, 5-D maps over [blocks, block_size, kv_heads,
 // D/64, 64] of each cache, 128-byte swizzle, no multicast) completing on the
 // stage's mbarrier; the waits are bounded in wall time like every wait of this
@@ -38,8 +40,8 @@
 namespace nib {
 
 constexpr int kMmaWarps = 4;
-constexpr int kMmaStages = 3;
-constexpr int kMmaTile = 16;  // tokens per tile
+constexpr int kMmaStages = 2;  // ring stages per warp: 3 CTAs (12 warps) per SM fit
+constexpr int kMmaTile = 16;   // tokens per tile
 
 struct MmaDecodeParams {
   const void* q;
@@ -116,7 +118,7 @@ __device__ __forceinline__ float ex2_fast(float x) {
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kMmaWarps * 32)
+__global__ void __launch_bounds__(kMmaWarps * 32, 3)
 decode_attention_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                             const MmaDecodeParams p) {
   constexpr int KS = D / 16;          // k-steps of Q K^T
