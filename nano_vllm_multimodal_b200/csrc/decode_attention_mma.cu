@@ -19,10 +19,10 @@
 // Each warp owns every kMmaWarps-th tile of the CTA's range and a private ring
 // of kMmaStages (2) shared-memory stages, so 3 CTAs (12 warps) fit on an SM:
 // with 3 stages and 2 CTAs per SM the GQA-8 C2 decode took 0.210 ms instead of
-// 0.203 ms. Lane 0 loads a tile with two TMA tensor
-// copies (cp.async.bulk.tensor, 5-D maps over [blocks, block_size, kv_heads,
-// D/64, 64] of each cache, 128-byte swizzle, no multicast) completing on the
-// stage's mbarrier; the waits are bounded in wall time like every wait of this
+// 0.203 ms. Lane 0 loads a tile with two TMA tensor copies per 64-element
+// half of the head, one from each cache (cp.async.bulk.tensor, 5-D maps over
+// [blocks, block_size, kv_heads, D/64, 64], 128-byte swizzle, no multicast),
+// completing on the stage's mbarrier; the waits are bounded in wall time like every wait of this
 // library (on timeout: NIB_DEV_TIMEOUT, wait for the warp's other copies,
 // return). Fragments come from shared memory with ldmatrix (.trans for V);
 // the swizzle keeps those reads free of bank conflicts. Scores are kept in
@@ -58,13 +58,18 @@ struct MmaDecodeParams {
   unsigned int* status;
 };
 
-// byte offset of (token t, element d) inside a stage's K or V tile: 128-byte
-// rows (row = t * D/64 + d/64) whose 16-byte chunks are XOR-swizzled by row % 8,
-// which is how a SWIZZLE_128B tensor copy lays the box out
+// byte offset of (token t, element d) inside a stage's K or V tile. The tile is
+// D/64 regions (one per 64-element half of the head, one tensor copy each) of
+// kMmaTile 128-byte rows, row = token, whose 16-byte chunks are XOR-swizzled by
+// row % 8 - how a SWIZZLE_128B tensor copy lays its box out. An ldmatrix phase
+// reads the same chunk of 8 consecutive tokens: 8 different rows, 8 different
+// swizzled chunks, no bank conflict. (With both halves of a token in one box,
+// consecutive tokens sit 2 rows apart and every phase conflicts 2-way: 48% of
+// the shared-memory wavefronts in the first version of this kernel.)
 template <int D>
 __device__ __forceinline__ uint32_t swz(int t, int d) {
-  const int row = t * (D / 64) + (d >> 6);
-  return static_cast<uint32_t>(row * 128 + ((((d & 63) >> 3) ^ (row & 7)) << 4) + (d & 7) * 2);
+  return static_cast<uint32_t>((d >> 6) * (kMmaTile * 128) + t * 128 + ((((d & 63) >> 3) ^ (t & 7)) << 4) +
+                               (d & 7) * 2);
 }
 
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
@@ -198,8 +203,11 @@ decode_attention_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __gr
       if (ok) {
         const int off = static_cast<int>(t0 - bi * p.block_size);
         const uint32_t dst = ring + st * kStageBytes;
-        tma_load_5d(dst, &kmap, 0, 0, kvh, off, blk, &bars[w][st]);
-        tma_load_5d(dst + kTileBytes, &vmap, 0, 0, kvh, off, blk, &bars[w][st]);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {  // one region per 64-element half
+          tma_load_5d(dst + c * kMmaTile * 128, &kmap, 0, c, kvh, off, blk, &bars[w][st]);
+          tma_load_5d(dst + kTileBytes + c * kMmaTile * 128, &vmap, 0, c, kvh, off, blk, &bars[w][st]);
+        }
       }
       ok_bits = (ok_bits & ~(1u << st)) | (static_cast<uint32_t>(ok) << st);
     }
@@ -229,11 +237,12 @@ decode_attention_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __gr
     if (t0 < t_begin || t0 + kMmaTile > t_end) {
       unsigned char* kg = dsm + (kt - base_all);
       for (int e = lane; e < kMmaTile * (D / 8); e += 32) {  // 16-byte units of one tile
-        const int t = e / (D / 8);
+        const int t = e % kMmaTile;  // a token's row in each region (the chunk order within does not matter)
         if (t0 + t < t_begin || t0 + t >= t_end) {
-          const int u = e % (D / 8);
-          *reinterpret_cast<uint4*>(kg + t * D * 2 + u * 16) = make_uint4(0, 0, 0, 0);
-          *reinterpret_cast<uint4*>(kg + kTileBytes + t * D * 2 + u * 16) = make_uint4(0, 0, 0, 0);
+          const int u = e / kMmaTile;  // (region, chunk)
+          const uint32_t at = (u >> 3) * (kMmaTile * 128) + t * 128 + (u & 7) * 16;
+          *reinterpret_cast<uint4*>(kg + at) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(kg + kTileBytes + at) = make_uint4(0, 0, 0, 0);
         }
       }
       __syncwarp();
@@ -404,7 +413,7 @@ static int make_cache_map(CUtensorMap* map, const nib_decode_attention_args& a, 
   const cuuint64_t strides[4] = {128, static_cast<cuuint64_t>(a.cache_head_stride * 2),
                                  static_cast<cuuint64_t>(a.cache_slot_stride * 2),
                                  static_cast<cuuint64_t>(a.cache_block_stride * 2)};
-  const cuuint32_t box[5] = {64, static_cast<cuuint32_t>(a.head_dim / 64), 1, kMmaTile, 1};
+  const cuuint32_t box[5] = {64, 1, 1, kMmaTile, 1};  // one 64-element half of the head per copy
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   const CUtensorMapDataType dt =
       a.dtype == NIB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
