@@ -33,7 +33,13 @@ def load_ops() -> None:
 
         try:
             if not _build.up_to_date():
-                _build.build()
+                # one process builds at a time (ranks of a multi-GPU run start together);
+                # the others find the stamp current once they hold the lock
+                import fcntl
+                with open(PKG / ".build.lock", "w") as lock:
+                    fcntl.flock(lock, fcntl.LOCK_EX)
+                    if not _build.up_to_date():
+                        _build.build()
         except Exception as exc:  # pragma: no cover - exercised only on broken toolchains
             raise RuntimeError(
                 "nano_vllm_multimodal_b200: building the sm_100a CUDA extension failed; "

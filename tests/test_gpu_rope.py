@@ -222,3 +222,39 @@ def test_module_forward_and_cos_sin():
         mod(d["positions"][:2].cuda(), q.cuda(), k.cuda())
     with pytest.raises(ValueError, match="rotary positions must match"):
         mod(d["positions"][:, :5].cuda(), q.cuda(), k.cuda())
+
+
+@pytest.mark.parametrize("rope_kind,nq,nkv,dim,tokens", [
+    ("table", 16, 8, 128, 4099), ("interleaved", 16, 8, 128, 3000), ("chunked", 16, 2, 128, 8312),
+    ("table", 14, 2, 64, 777), ("interleaved", 8, 8, 256, 300), ("chunked", 28, 4, 128, 1)])
+def test_rotary_only_kernels_agree(rope_kind, nq, nkv, dim, tokens):
+    """Rotary alone (the rotary modules' forward): the automatic choice (the
+    warp-per-token rotary kernel) is bit-identical to the pipelined and the
+    register-staged prologue kernels on strided q/k views of a qkv row, and to
+    the oracle given the kernel's cos/sin."""
+    g = torch.Generator().manual_seed(tokens + dim)
+    qkv = torch.randn(tokens, (nq + 2 * nkv) * dim, generator=g).to(torch.bfloat16)
+    q = qkv[:, :nq * dim].view(tokens, nq, dim)
+    k = qkv[:, nq * dim:(nq + nkv) * dim].view(tokens, nkv, dim)
+    half = dim // 2
+    if rope_kind == "table":
+        table = O.rope_cos_sin_cache(dim, 40960, 1e6)
+        pos = torch.randint(0, 40960, (tokens,), generator=g)
+        kw = dict(rope_mode=ops.ROPE_TABLE, cos_sin_cache=table.cuda())
+        eq, ek = O.apply_rope(pos, q, k, table)
+    else:
+        sections = (half - 2 * (half // 3), half // 3, half // 3) if rope_kind == "interleaved" else \
+            (half // 4, half // 4, half - 2 * (half // 4))
+        inv = O.mrope_inv_freq(dim, 5e6)
+        pos = torch.randint(0, 32768, (3, tokens), generator=g)
+        mode = ops.ROPE_MROPE_INTERLEAVED if rope_kind == "interleaved" else ops.ROPE_MROPE_CHUNKED
+        kw = dict(rope_mode=mode, inv_freq=inv.cuda(), sections=sections)
+        c, s = ops.mrope_cos_sin(pos.cuda(), inv.cuda(), torch.bfloat16)
+        eq, ek = O.apply_mrope(q, k, c.cpu(), s.cpu(), sections, rope_kind)
+    gq, gk = qkv.cuda()[:, :nq * dim].view(tokens, nq, dim), qkv.cuda()[:, nq * dim:(nq + nkv) * dim].view(tokens, nkv, dim)
+    outs = [ops.qk_prologue(gq, gk, positions=pos.cuda(), variant=v, **kw) for v in (0, 1, 2)]
+    for v, (aq, ak) in zip((1, 2), outs[1:]):
+        assert_bitexact(outs[0][0], aq.cpu(), f"q auto vs variant {v}")
+        assert_bitexact(outs[0][1], ak.cpu(), f"k auto vs variant {v}")
+    assert_bitexact(outs[0][0], eq, "q vs oracle")
+    assert_bitexact(outs[0][1], ek, "k vs oracle")
