@@ -236,16 +236,17 @@ typedef struct {
   const int32_t* slot_mapping; /* [tokens], -1 = skip */
   int64_t num_slots, cache_slot_stride;
   unsigned int* status;
-  /* 0 = choose automatically; 1 = register-staged kernel (any strides);
-     2 = bulk-copy pipelined kernel (q/k/v consecutive head ranges of one row) */
+  /* 0 = choose automatically (rotary alone, no norm and no store: a warp-per-token
+     rotary kernel; otherwise one of the two below); 1 = register-staged kernel (any
+     strides); 2 = bulk-copy pipelined kernel (q/k/v consecutive head ranges of one row) */
   int32_t variant;
 } nib_qk_prologue_args;
 
 /* Per token: optional per-head RMSNorm of q and k, rotary embedding of the
  * normalised q and k, rotated q/k written to q_out/k_out, and (when
  * key_cache != NULL and slot >= 0) rotated k and raw v written to the paged
- * caches. head_dim must be 64, 128 or 256. Both kernel
- * variants compute bit-identical results.
+ * caches. head_dim must be 64, 128 or 256. All kernel variants compute
+ * bit-identical results.
  * Replaces, fused, the sequence
  *   q_norm / k_norm        nanovllm/models/qwen3.py:82-84, qwen3_vl.py:170-171
  *   RotaryEmbedding.forward  nanovllm/layers/rotary_embedding.py:37-48

@@ -39,4 +39,8 @@ struct PipeLayout {
 bool prologue_pipe_eligible(const nib_qk_prologue_args& a);
 int launch_prologue_pipe(const nib_qk_prologue_args& a, cudaStream_t st);
 
+// rotary alone (no norm, no store): the warp-per-token kernel of rope_rows.cu
+bool rope_rows_eligible(const nib_qk_prologue_args& a);
+int launch_rope_rows(const nib_qk_prologue_args& a, cudaStream_t st);
+
 }  // namespace nib

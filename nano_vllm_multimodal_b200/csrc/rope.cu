@@ -561,6 +561,9 @@ extern "C" int nib_qk_prologue(const nib_qk_prologue_args* args, void* stream) {
   const bool pipe_ok = prologue_pipe_eligible(a);
   NIB_SUPPORT(a.variant != 2 || pipe_ok, "qk_prologue: the pipelined variant needs q/k/v as consecutive "
               "head ranges of one 16-byte aligned bf16/fp16 row");
+  // rotary alone (the rotary modules' forward): one warp per token, all loads first; the
+  // pipelined kernel reached 69-81% of the copy bandwidth on these launches
+  if (a.variant == 0 && rope_rows_eligible(a)) return launch_rope_rows(a, st);
   if (a.variant == 2 || (a.variant == 0 && pipe_ok && a.tokens >= kPipeMinTokens))
     return launch_prologue_pipe(a, st);
   NIB_DISPATCH(a.dtype, T, {

@@ -251,7 +251,12 @@ def test_rotary_only_kernels_agree(rope_kind, nq, nkv, dim, tokens):
         kw = dict(rope_mode=mode, inv_freq=inv.cuda(), sections=sections)
         c, s = ops.mrope_cos_sin(pos.cuda(), inv.cuda(), torch.bfloat16)
         eq, ek = O.apply_mrope(q, k, c.cpu(), s.cpu(), sections, rope_kind)
-    gq, gk = qkv.cuda()[:, :nq * dim].view(tokens, nq, dim), qkv.cuda()[:, nq * dim:(nq + nkv) * dim].view(tokens, nkv, dim)
+    # one device row: q and k are consecutive head ranges of it, with the row's token stride
+    # even for a single token (view() picks its own stride for a size-1 dimension)
+    gqkv = qkv.cuda()
+    row = gqkv.stride(0)
+    gq = gqkv.as_strided((tokens, nq, dim), (row, dim, 1), 0)
+    gk = gqkv.as_strided((tokens, nkv, dim), (row, dim, 1), nq * dim)
     outs = [ops.qk_prologue(gq, gk, positions=pos.cuda(), variant=v, **kw) for v in (0, 1, 2)]
     for v, (aq, ak) in zip((1, 2), outs[1:]):
         assert_bitexact(outs[0][0], aq.cpu(), f"q auto vs variant {v}")
