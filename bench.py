@@ -534,16 +534,27 @@ def _time_graph(calls, reps=24):
     return best
 
 
+def flush_l2(buf):
+    """Flush the L2 between timed calls: write ``buf`` (4x the 126 MB L2), then read
+    it back. The write evicts every earlier line; the read evicts the write's own
+    dirty lines, so the timed call starts from a clean L2 holding none of its
+    inputs and does not pay for writing 126 MB of the flush back to DRAM (13.5 us
+    of a 0.2 ms decode-attention call). Both run outside the timed events."""
+    buf.zero_()
+    buf.view(torch.int64).sum()
+
+
 def _time_op(fn, reps=20, warmup=3, flush=None):
     """Average ms of ``fn`` with CUDA events around each call; ``flush`` (a
-    buffer larger than L2) is overwritten between calls, outside the events."""
+    buffer larger than L2) flushes the L2 between calls (``flush_l2``), outside
+    the events."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     total = 0.0
     for _ in range(reps):
         if flush is not None:
-            flush.zero_()
+            flush_l2(flush)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         fn()
@@ -774,7 +785,7 @@ def rows_flushed_rounds(flush, device, rounds=3):
     ms = dict.fromkeys(fns, 0.0)
     for r in range(rounds):
         for name, fn in fns.items():
-            flush.zero_()
+            flush_l2(flush)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             fn()

@@ -122,6 +122,129 @@ __device__ __forceinline__ float ex2_fast(float x) {
   return y;
 }
 
+// Zero the K and V rows of the tokens outside [lo, hi) (tile-relative) of one
+// stage, whatever the cache holds there: their scores are masked, but 0 x NaN
+// would still reach the sums. The fence orders these generic writes before
+// the stage's next tensor copy.
+template <int D>
+__device__ __forceinline__ void zero_rows(unsigned char* kg, int lo, int hi, int lane) {
+  constexpr uint32_t kTileBytes = kMmaTile * D * 2;
+  for (int e = lane; e < kMmaTile * (D / 8); e += 32) {  // 16-byte units of one tile
+    const int t = e % kMmaTile;  // a token's row in each region (the chunk order within does not matter)
+    if (t < lo || t >= hi) {
+      const int u = e / kMmaTile;  // (region, chunk)
+      const uint32_t at = (u >> 3) * (kMmaTile * 128) + t * 128 + (u & 7) * 16;
+      *reinterpret_cast<uint4*>(kg + at) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(kg + kTileBytes + at) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  fence_proxy_async();
+  __syncwarp();
+}
+
+// Q fragments of one (request, kv head): the A operand, rows = the kv head's q
+// heads, zero past the group.
+template <typename T, int D>
+__device__ __forceinline__ void load_q_frags(uint32_t (&qa)[D / 16][4], const T* qb, int64_t q_hs, int first_head,
+                                             int group, int lane) {
+  const int r0 = lane >> 2, cq = (lane & 3) * 2;
+  const bool ok0 = r0 < group, ok1 = r0 + 8 < group;
+  const T* q0 = qb + static_cast<int64_t>(first_head + (ok0 ? r0 : 0)) * q_hs;
+  const T* q1 = qb + static_cast<int64_t>(first_head + (ok1 ? r0 + 8 : 0)) * q_hs;
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks) {
+    const int k = ks * 16 + cq;
+    qa[ks][0] = ok0 ? __ldg(reinterpret_cast<const uint32_t*>(q0 + k)) : 0u;
+    qa[ks][1] = ok1 ? __ldg(reinterpret_cast<const uint32_t*>(q1 + k)) : 0u;
+    qa[ks][2] = ok0 ? __ldg(reinterpret_cast<const uint32_t*>(q0 + k + 8)) : 0u;
+    qa[ks][3] = ok1 ? __ldg(reinterpret_cast<const uint32_t*>(q1 + k + 8)) : 0u;
+  }
+}
+
+// One 16-token tile of a stage (K at kt, V at kt + tile bytes) into the online
+// softmax state of rows r0 (a) and r0 + 8 (b): S = Q K^T, scores of tokens
+// outside [lo, hi) (tile-relative) masked, then O += P V.
+template <typename T, int D>
+__device__ __forceinline__ void mma_tile(const uint32_t (&qa)[D / 16][4], uint32_t kt, int lo, int hi, float qscale,
+                                         float (&o)[D / 8][4], float& m_a, float& m_b, float& l_a, float& l_b,
+                                         int lane) {
+  constexpr int KS = D / 16;
+  constexpr int ND = D / 8;
+  const uint32_t vt = kt + kMmaTile * D * 2;
+  const int cq = (lane & 3) * 2;
+  // ---- S = Q K^T (2 n-tiles of 8 tokens)
+  float s[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KS; ks += 2) {
+      uint32_t kb[4];
+      // matrices (tokens 8nt..8nt+7) x (d chunks 2ks .. 2ks+3): lane L gives row L%8 of matrix L/8
+      ldsm_x4(kt + swz<D>(nt * 8 + (lane & 7), (ks * 2 + (lane >> 3)) * 8), kb);
+      mma16816<T>(s[nt], qa[ks], kb[0], kb[1]);
+      mma16816<T>(s[nt], qa[ks + 1], kb[2], kb[3]);
+    }
+  }
+  // ---- online softmax (log2 domain); mask tokens outside the range
+  float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int t = nt * 8 + cq + c;
+      const bool in = t >= lo && t < hi;
+      s[nt][c] = in ? s[nt][c] * qscale : -INFINITY;
+      s[nt][c + 2] = in ? s[nt][c + 2] * qscale : -INFINITY;
+      mx_a = fmaxf(mx_a, s[nt][c]);
+      mx_b = fmaxf(mx_b, s[nt][c + 2]);
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < 4; off <<= 1) {
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+  }
+  const float na = fmaxf(m_a, mx_a), nb = fmaxf(m_b, mx_b);
+  const float ra = na == -INFINITY ? 1.f : ex2_fast(m_a - na);
+  const float rb = nb == -INFINITY ? 1.f : ex2_fast(m_b - nb);
+  m_a = na;
+  m_b = nb;
+  float pa[2][2], pb[2][2];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      pa[nt][c] = na == -INFINITY ? 0.f : ex2_fast(s[nt][c] - na);
+      pb[nt][c] = nb == -INFINITY ? 0.f : ex2_fast(s[nt][c + 2] - nb);
+    }
+  }
+  l_a = l_a * ra + (pa[0][0] + pa[0][1]) + (pa[1][0] + pa[1][1]);
+  l_b = l_b * rb + (pb[0][0] + pb[0][1]) + (pb[1][0] + pb[1][1]);
+#pragma unroll
+  for (int n = 0; n < ND; ++n) {
+    o[n][0] *= ra;
+    o[n][1] *= ra;
+    o[n][2] *= rb;
+    o[n][3] *= rb;
+  }
+  // P as the A fragment of one 16-token k-step (the C layout of two n-tiles)
+  uint32_t pf[4];
+  pf[0] = pack2<T>(pa[0][0], pa[0][1]);
+  pf[1] = pack2<T>(pb[0][0], pb[0][1]);
+  pf[2] = pack2<T>(pa[1][0], pa[1][1]);
+  pf[3] = pack2<T>(pb[1][0], pb[1][1]);
+  // ---- O += P V (V^T fragments by ldmatrix.trans: rows = tokens, 8 d values each)
+#pragma unroll
+  for (int n2 = 0; n2 < ND; n2 += 2) {
+    uint32_t vb[4];
+    // matrices: (tokens 0-7, d chunk n2), (tokens 8-15, n2), (0-7, n2+1), (8-15, n2+1)
+    ldsm_x4_t(vt + swz<D>((lane & 7) + ((lane >> 3) & 1) * 8, (n2 + (lane >> 4)) * 8), vb);
+    mma16816<T>(o[n2], pf, vb[0], vb[1]);
+    mma16816<T>(o[n2 + 1], pf, vb[2], vb[3]);
+  }
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kMmaWarps * 32, 3)
 decode_attention_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
@@ -161,23 +284,9 @@ decode_attention_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __gr
   const int64_t n_tiles = t_end > t_begin ? (t_end + kMmaTile - 1) / kMmaTile - tile0 : 0;
   const int64_t n_mine = n_tiles > w ? (n_tiles - w + kMmaWarps - 1) / kMmaWarps : 0;  // warp-uniform
 
-  // Q as A fragments (rows = the kv head's q heads, zero past the group)
   const int r0 = lane >> 2, cq = (lane & 3) * 2;
   uint32_t qa[KS][4];
-  {
-    const T* qb = static_cast<const T*>(p.q) + b * p.q_bs;
-    const bool ok0 = r0 < p.group, ok1 = r0 + 8 < p.group;
-    const T* q0 = qb + static_cast<int64_t>(kvh * p.group + (ok0 ? r0 : 0)) * p.q_hs;
-    const T* q1 = qb + static_cast<int64_t>(kvh * p.group + (ok1 ? r0 + 8 : 0)) * p.q_hs;
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-      const int k = ks * 16 + cq;
-      qa[ks][0] = ok0 ? __ldg(reinterpret_cast<const uint32_t*>(q0 + k)) : 0u;
-      qa[ks][1] = ok1 ? __ldg(reinterpret_cast<const uint32_t*>(q1 + k)) : 0u;
-      qa[ks][2] = ok0 ? __ldg(reinterpret_cast<const uint32_t*>(q0 + k + 8)) : 0u;
-      qa[ks][3] = ok1 ? __ldg(reinterpret_cast<const uint32_t*>(q1 + k + 8)) : 0u;
-    }
-  }
+  load_q_frags<T, D>(qa, static_cast<const T*>(p.q) + b * p.q_bs, p.q_hs, kvh * p.group, p.group, lane);
 
   float o[ND][4];
 #pragma unroll
@@ -229,96 +338,13 @@ decode_attention_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __gr
     }
     const bool ok = (__shfl_sync(0xffffffffu, ok_bits, 0) >> st) & 1u;
     const int64_t t0 = (tile0 + w + i * kMmaWarps) * kMmaTile;
-    const uint32_t kt = ring + st * kStageBytes, vt = kt + kTileBytes;
+    const uint32_t kt = ring + st * kStageBytes;
     if (!ok) continue;  // bad block id: its tokens take no part
-    // tokens of this tile outside [t_begin, t_end) (the first and last tile):
-    // zero their K and V rows, whatever the cache holds there (the scores are
-    // masked too, but 0 x NaN would still reach the sums)
-    if (t0 < t_begin || t0 + kMmaTile > t_end) {
-      unsigned char* kg = dsm + (kt - base_all);
-      for (int e = lane; e < kMmaTile * (D / 8); e += 32) {  // 16-byte units of one tile
-        const int t = e % kMmaTile;  // a token's row in each region (the chunk order within does not matter)
-        if (t0 + t < t_begin || t0 + t >= t_end) {
-          const int u = e / kMmaTile;  // (region, chunk)
-          const uint32_t at = (u >> 3) * (kMmaTile * 128) + t * 128 + (u & 7) * 16;
-          *reinterpret_cast<uint4*>(kg + at) = make_uint4(0, 0, 0, 0);
-          *reinterpret_cast<uint4*>(kg + kTileBytes + at) = make_uint4(0, 0, 0, 0);
-        }
-      }
-      __syncwarp();
-    }
-
-    // ---- S = Q K^T (2 n-tiles of 8 tokens)
-    float s[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < KS; ks += 2) {
-        uint32_t kb[4];
-        // matrices (tokens 8nt..8nt+7) x (d chunks 2ks .. 2ks+3): lane L gives row L%8 of matrix L/8
-        ldsm_x4(kt + swz<D>(nt * 8 + (lane & 7), (ks * 2 + (lane >> 3)) * 8), kb);
-        mma16816<T>(s[nt], qa[ks], kb[0], kb[1]);
-        mma16816<T>(s[nt], qa[ks + 1], kb[2], kb[3]);
-      }
-    }
-    // ---- online softmax (log2 domain); mask tokens outside the range
-    float mx_a = -INFINITY, mx_b = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int64_t t = t0 + nt * 8 + cq + c;
-        const bool in = t >= t_begin && t < t_end;
-        s[nt][c] = in ? s[nt][c] * p.qscale : -INFINITY;
-        s[nt][c + 2] = in ? s[nt][c + 2] * p.qscale : -INFINITY;
-        mx_a = fmaxf(mx_a, s[nt][c]);
-        mx_b = fmaxf(mx_b, s[nt][c + 2]);
-      }
-    }
-#pragma unroll
-    for (int off = 1; off < 4; off <<= 1) {
-      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
-      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
-    }
-    const float na = fmaxf(m_a, mx_a), nb = fmaxf(m_b, mx_b);
-    const float ra = na == -INFINITY ? 1.f : ex2_fast(m_a - na);
-    const float rb = nb == -INFINITY ? 1.f : ex2_fast(m_b - nb);
-    m_a = na;
-    m_b = nb;
-    float pa[2][2], pb[2][2];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        pa[nt][c] = na == -INFINITY ? 0.f : ex2_fast(s[nt][c] - na);
-        pb[nt][c] = nb == -INFINITY ? 0.f : ex2_fast(s[nt][c + 2] - nb);
-      }
-    }
-    l_a = l_a * ra + (pa[0][0] + pa[0][1]) + (pa[1][0] + pa[1][1]);
-    l_b = l_b * rb + (pb[0][0] + pb[0][1]) + (pb[1][0] + pb[1][1]);
-#pragma unroll
-    for (int n = 0; n < ND; ++n) {
-      o[n][0] *= ra;
-      o[n][1] *= ra;
-      o[n][2] *= rb;
-      o[n][3] *= rb;
-    }
-    // P as the A fragment of one 16-token k-step (the C layout of two n-tiles)
-    uint32_t pf[4];
-    pf[0] = pack2<T>(pa[0][0], pa[0][1]);
-    pf[1] = pack2<T>(pb[0][0], pb[0][1]);
-    pf[2] = pack2<T>(pa[1][0], pa[1][1]);
-    pf[3] = pack2<T>(pb[1][0], pb[1][1]);
-    // ---- O += P V (V^T fragments by ldmatrix.trans: rows = tokens, 8 d values each)
-#pragma unroll
-    for (int n2 = 0; n2 < ND; n2 += 2) {
-      uint32_t vb[4];
-      // matrices: (tokens 0-7, d chunk n2), (tokens 8-15, n2), (0-7, n2+1), (8-15, n2+1)
-      ldsm_x4_t(vt + swz<D>((lane & 7) + ((lane >> 3) & 1) * 8, (n2 + (lane >> 4)) * 8), vb);
-      mma16816<T>(o[n2], pf, vb[0], vb[1]);
-      mma16816<T>(o[n2 + 1], pf, vb[2], vb[3]);
-    }
+    // the tile's tokens in [t_begin, t_end), tile-relative (only the first and last tile are partial)
+    const int lo = t_begin > t0 ? static_cast<int>(t_begin - t0) : 0;
+    const int hi = t_end - t0 < kMmaTile ? static_cast<int>(t_end - t0) : kMmaTile;
+    if (lo > 0 || hi < kMmaTile) zero_rows<D>(dsm + (kt - base_all), lo, hi, lane);
+    mma_tile<T, D>(qa, kt, lo, hi, p.qscale, o, m_a, m_b, l_a, l_b, lane);
     __syncwarp();  // every lane has read the stage before it is refilled
   }
 

@@ -50,12 +50,14 @@ def timing_inputs(device):
 
 
 def time_ms(fn, flush, reps=10, warmup=3):
-    """Median of one call at a time, each after writing a 512 MB buffer (the L2 flushed)."""
+    """Median of one call at a time, each after writing a 512 MB buffer and reading it
+    back (the L2 flushed and left clean, so no call pays for the flush's write-back)."""
     for _ in range(warmup):
         fn()
     times = []
     for _ in range(reps):
         flush.zero_()
+        flush.view(torch.int64).sum()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         fn()

@@ -153,6 +153,36 @@ def test_long_contexts_split_across_ctas_and_strided_q():
         _close_to_oracle(out, expect, f"split contexts, variant {variant}", vabs)
 
 
+@pytest.mark.parametrize("nq,nkv,dim,bs", [(16, 2, 128, 64), (16, 8, 128, 256), (8, 1, 64, 32)])
+def test_many_ragged_requests(nq, nkv, dim, bs):
+    """160 requests of ragged lengths: many one-tile contexts, two empty ones, long
+    ones split over CTAs, NaN in every stale slot past a context. The default
+    (tensor-core) kernel and the CUDA-core kernel against the oracle; empty
+    contexts give zeros; two calls give the same bits."""
+    g = torch.Generator().manual_seed(nq * 100 + nkv * 10 + dim)
+    lens = torch.randint(1, 1200, (160,), generator=g)
+    lens[::7] = torch.randint(1, 17, (lens[::7].numel(),), generator=g)
+    lens[[5, 99]] = 0
+    lens[[50, 51]] = torch.tensor([9000, 4097])
+    lens = lens.tolist()
+    q, kc, vc, cl, tb = _case(nq + nkv + dim, len(lens), nq, nkv, dim, bs, lens)
+    for b, n in enumerate(lens):
+        last = int(tb[b, max(n - 1, 0) // bs])
+        kc[last, n % bs or (bs if n else 0):] = float("nan")
+        vc[last, n % bs or (bs if n else 0):] = float("nan")
+    scale = dim ** -0.5
+    args = (q.cuda(), kc.cuda(), vc.cuda(), cl.cuda(), tb.cuda(), scale)
+    out = ops.decode_attention(*args)
+    assert not torch.isnan(out).any()
+    expect, vabs = _oracle(q, kc, vc, cl, tb, scale)
+    _close_to_oracle(out, expect, f"ragged {nq}/{nkv} D{dim}", vabs)
+    for b in (5, 99):
+        assert not out[b].any(), "an empty context gives zeros"
+    fma = ops.decode_attention(*args, variant=ops.DECODE_CUDA_CORES)
+    _close_to_oracle(fma, expect, f"CUDA cores, ragged {nq}/{nkv} D{dim}")
+    assert torch.equal(ops.decode_attention(*args), out), "deterministic"
+
+
 def test_flash_attn_shaped_drop_in():
     q, kc, vc, cl, tb = _case(5, 4, 16, 8, 128, 256, [3, 700, 256, 1])
     qg, kg, vg, cg, tg = q.cuda(), kc.cuda(), vc.cuda(), cl.cuda(), tb.cuda()
