@@ -1328,13 +1328,16 @@ def ours_arm(args, rank, world, local):
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded, C5 shapes, random-init norm weights)",
         "config": config_block(args, world),
+        # the long blocks first, so that a record keeping only the end of the line still holds the
+        # roofline, e2e, CPU baseline, clocks and the per-kernel figures
+        "components": components, "configs": configs,
         "hbm": {"algorithmic_bytes_per_step": step_bytes_job,
                 "gbs": step_bytes_job / (ms_max / args.steps / 1000.0) / 1e9,
                 "frac_of_peak": step_bytes_job / (ms_max / args.steps / 1000.0) / 1e9 / (hbm_peak * world),
                 "peak_gbs": hbm_peak * world, "peak_note": "measured per-GPU copy bandwidth x GPUs"},
-        "roofline": roofline, "kernels": per_kernel, "configs": configs, "components": components,
-        "e2e": e2e, "cpu_baseline": cpu, "clocks": clock,
+        "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clock,
         "gpu_launches": launches_per_step(args.layers, inp["gather_seqs"]) * args.steps,
+        "kernels": per_kernel,
     }
     print(json.dumps(line), flush=True)
     return 0
