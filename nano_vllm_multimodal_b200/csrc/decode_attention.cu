@@ -402,13 +402,18 @@ static DecodePlan decode_plan(const nib_decode_attention_args& a) {
   pl.warps = pl.head_groups * pl.token_groups;
   pl.mma = a.variant != 1 && decode_mma_eligible(a);
   // splits: enough CTAs for every SM, at least 256 tokens per split (tensor-core
-  // kernel: at least 64, one 16-token tile per warp). The tensor-core kernel asks
-  // for 16 CTAs per SM (about 5 waves at 3 resident): at C2 decode with GQA 8
-  // (512 request x kv-head pairs, contexts U[1, 8192]) 4 gave 0.218 ms, 8 and 16
-  // 0.210 ms, 32 0.238 ms; with GQA 2 (2,048 pairs) 16 was 1.5% faster than 4.
+  // kernel: at least 64, one 16-token tile per warp). The tensor-core kernel's
+  // splits shrink linearly toward the last one (decode_attention_mma.cu), which
+  // puts small CTAs in the grid's last wave; it asks for 12 CTAs per SM (about 4
+  // waves at 3 resident) and at least 2 splits. Measured on C2's contexts
+  // (U[1, 8192], ms per call, CTAs per SM wanted 8 / 12 / 16 / 24): GQA 8 with
+  // 256 requests 0.191 / 0.183 / 0.184 / 0.191; 8/1 heads 0.102 / 0.104 / 0.110 /
+  // 0.120; 64 requests of up to 32,768 tokens 0.183 / 0.181 / 0.185 / 0.192; GQA 2
+  // with 256 requests 0.658 with one split, 0.641 with two.
   const int64_t ctas = a.batch * a.num_kv_heads;
-  const int64_t want = (pl.mma ? 16LL : 4LL) * sm_count();
+  const int64_t want = (pl.mma ? 12LL : 4LL) * sm_count();
   int64_t s = ctas >= want ? 1 : (want + ctas - 1) / ctas;
+  if (pl.mma && s < 2) s = 2;
   const int64_t max_len = a.max_context_len > 0 ? a.max_context_len : a.max_blocks_per_seq * a.block_size;
   const int64_t by_len = (max_len + (pl.mma ? 63 : 255)) / (pl.mma ? 64 : 256);
   if (kDecodeSplitTokens > 0) {

@@ -277,9 +277,16 @@ decode_attention_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __gr
     if (threadIdx.x == 0 && split == 0) flag(p.status, NIB_DEV_BAD_INDEX);
     len = len < 0 ? 0 : cap;
   }
-  const int64_t chunk = (len + p.splits - 1) / p.splits;
-  const int64_t t_begin = split * chunk;
-  const int64_t t_end = t_begin + chunk < len ? t_begin + chunk : len;
+  // Split boundaries: the splits of a context shrink linearly toward the last one
+  // (split y gets a share s - y of s + (s-1) + ... + 1), and the grid's rows are
+  // dispatched in split order, so its final wave holds the smallest CTAs.
+  auto split_start = [&](int y) -> int64_t {
+    const int64_t sp = p.splits;
+    const int64_t before = y * sp - static_cast<int64_t>(y) * (y - 1) / 2;
+    return len * before / (sp * (sp + 1) / 2);
+  };
+  const int64_t t_begin = split_start(split);
+  const int64_t t_end = split_start(split + 1);
   const int64_t tile0 = t_begin / kMmaTile;
   const int64_t n_tiles = t_end > t_begin ? (t_end + kMmaTile - 1) / kMmaTile - tile0 : 0;
   const int64_t n_mine = n_tiles > w ? (n_tiles - w + kMmaWarps - 1) / kMmaWarps : 0;  // warp-uniform

@@ -216,7 +216,8 @@ def test_drop_in_captures_in_a_cuda_graph(batch):
     """ModelRunner captures its decode steps in CUDA graphs, attention included. The
     drop-in reads no device value on the host, so it captures; replays with new
     queries, context lengths and block tables written in place equal eager calls.
-    4 requests split their contexts over CTAs (partials in the workspace); 128 do not."""
+    4 requests split their contexts over many CTAs, 128 over two (partials in the
+    workspace, merged by a second launch inside the graph)."""
     nq, nkv, D, bs, width = 16, 8, 128, 256, 8
     g = torch.Generator().manual_seed(batch)
     nblocks = batch * width

@@ -224,16 +224,19 @@ def test_module_forward_and_cos_sin():
         mod(d["positions"][:, :5].cuda(), q.cuda(), k.cuda())
 
 
-@pytest.mark.parametrize("rope_kind,nq,nkv,dim,tokens", [
-    ("table", 16, 8, 128, 4099), ("interleaved", 16, 8, 128, 3000), ("chunked", 16, 2, 128, 8312),
-    ("table", 14, 2, 64, 777), ("interleaved", 8, 8, 256, 300), ("chunked", 28, 4, 128, 1)])
-def test_rotary_only_kernels_agree(rope_kind, nq, nkv, dim, tokens):
+@pytest.mark.parametrize("rope_kind,nq,nkv,dim,tokens,dtype", [
+    ("table", 16, 8, 128, 4099, torch.bfloat16), ("interleaved", 16, 8, 128, 3000, torch.bfloat16),
+    ("chunked", 16, 2, 128, 8312, torch.bfloat16), ("table", 14, 2, 64, 777, torch.bfloat16),
+    ("interleaved", 8, 8, 256, 300, torch.bfloat16), ("chunked", 28, 4, 128, 1, torch.bfloat16),
+    ("table", 16, 8, 128, 513, torch.float16), ("interleaved", 16, 8, 128, 700, torch.float16),
+    ("chunked", 16, 2, 64, 257, torch.float16)])
+def test_rotary_only_kernels_agree(rope_kind, nq, nkv, dim, tokens, dtype):
     """Rotary alone (the rotary modules' forward): the automatic choice (the
     warp-per-token rotary kernel) is bit-identical to the pipelined and the
     register-staged prologue kernels on strided q/k views of a qkv row, and to
     the oracle given the kernel's cos/sin."""
     g = torch.Generator().manual_seed(tokens + dim)
-    qkv = torch.randn(tokens, (nq + 2 * nkv) * dim, generator=g).to(torch.bfloat16)
+    qkv = torch.randn(tokens, (nq + 2 * nkv) * dim, generator=g).to(dtype)
     q = qkv[:, :nq * dim].view(tokens, nq, dim)
     k = qkv[:, nq * dim:(nq + nkv) * dim].view(tokens, nkv, dim)
     half = dim // 2
@@ -249,7 +252,7 @@ def test_rotary_only_kernels_agree(rope_kind, nq, nkv, dim, tokens):
         pos = torch.randint(0, 32768, (3, tokens), generator=g)
         mode = ops.ROPE_MROPE_INTERLEAVED if rope_kind == "interleaved" else ops.ROPE_MROPE_CHUNKED
         kw = dict(rope_mode=mode, inv_freq=inv.cuda(), sections=sections)
-        c, s = ops.mrope_cos_sin(pos.cuda(), inv.cuda(), torch.bfloat16)
+        c, s = ops.mrope_cos_sin(pos.cuda(), inv.cuda(), dtype)
         eq, ek = O.apply_mrope(q, k, c.cpu(), s.cpu(), sections, rope_kind)
     # one device row: q and k are consecutive head ranges of it, with the row's token stride
     # even for a single token (view() picks its own stride for a size-1 dimension)
