@@ -363,6 +363,8 @@ decode_attention_kernel(const DecodeParams p) {
 }
 
 // out[b, h, d] from the split partials (max-rescaled sums)
+constexpr int kCombineUnrolled = 8;  // split counts merged with one round of loads
+
 template <typename T, int D>
 __global__ void __launch_bounds__(D)
 decode_combine_kernel(const DecodeParams p) {
@@ -374,13 +376,37 @@ decode_combine_kernel(const DecodeParams p) {
   const int d = threadIdx.x;
   const float* ws = p.ws + bh * p.splits * SW;
   float M = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, ws[s * SW + D]);
   float L = 0.f, A = 0.f;
-  if (M != -INFINITY) {
-    for (int s = 0; s < p.splits; ++s) {
-      const float f = ex2f(ws[s * SW + D] - M);
-      L += ws[s * SW + D + 1] * f;
-      A += ws[s * SW + d] * f;
+  if (p.splits <= kCombineUnrolled) {
+    // every split's max, sum and element loaded at once: one memory round trip
+    float m[kCombineUnrolled], l[kCombineUnrolled], o[kCombineUnrolled];
+#pragma unroll
+    for (int s = 0; s < kCombineUnrolled; ++s) {
+      const bool in = s < p.splits;
+      m[s] = in ? ws[s * SW + D] : -INFINITY;
+      l[s] = in ? ws[s * SW + D + 1] : 0.f;
+      o[s] = in ? ws[s * SW + d] : 0.f;
+    }
+#pragma unroll
+    for (int s = 0; s < kCombineUnrolled; ++s) M = fmaxf(M, m[s]);
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int s = 0; s < kCombineUnrolled; ++s) {
+        if (s < p.splits) {  // the same sums, in the same order, as the loop below
+          const float f = ex2f(m[s] - M);
+          L += l[s] * f;
+          A += o[s] * f;
+        }
+      }
+    }
+  } else {
+    for (int s = 0; s < p.splits; ++s) M = fmaxf(M, ws[s * SW + D]);
+    if (M != -INFINITY) {
+      for (int s = 0; s < p.splits; ++s) {
+        const float f = ex2f(ws[s * SW + D] - M);
+        L += ws[s * SW + D + 1] * f;
+        A += ws[s * SW + d] * f;
+      }
     }
   }
   static_cast<T*>(p.out)[b * p.o_bs + h * p.o_hs + d] = Elem<T>::from_f(L > 0.f ? A / L : 0.f);
@@ -493,7 +519,7 @@ static int launch_decode(const nib_decode_attention_args& a, const DecodePlan& p
     configured[dev] = static_cast<int>(pl.smem);
   }
   ::nib::launch_k(kernel, grid, pl.warps * 32, pl.smem, st, p);
-  if (pl.splits > 1) ::nib::launch_k(decode_combine_kernel<T, D>, static_cast<unsigned>(a.batch * a.num_heads), D, 0, st, p);
+  if (pl.splits > 1) ::nib::launch_k_after(decode_combine_kernel<T, D>, static_cast<unsigned>(a.batch * a.num_heads), D, 0, st, p);
   return launch_status("decode_attention");
 }
 
@@ -507,7 +533,7 @@ static int launch_combine(const nib_decode_attention_args& a, int splits, cudaSt
   p.ws = static_cast<float*>(a.workspace);
   p.num_heads = a.num_heads;
   p.splits = splits;
-  ::nib::launch_k(decode_combine_kernel<T, D>, static_cast<unsigned>(a.batch * a.num_heads), D, 0, st, p);
+  ::nib::launch_k_after(decode_combine_kernel<T, D>, static_cast<unsigned>(a.batch * a.num_heads), D, 0, st, p);
   return launch_status("decode_attention (combine)");
 }
 

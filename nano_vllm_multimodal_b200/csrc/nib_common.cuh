@@ -37,8 +37,8 @@ bool pdl_enabled();
 void note_launch_error(cudaError_t e);  // reported by the next launch_status()
 
 template <typename... KArgs, typename... Args>
-inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                     Args&&... args) {
+inline void launch_k_pdl(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                         Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -48,9 +48,27 @@ inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = pdl ? 1 : 0;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
   if (e != cudaSuccess) note_launch_error(e);
+}
+
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     Args&&... args) {
+  launch_k_pdl(pdl_enabled(), kernel, grid, block, smem, st, std::forward<Args>(args)...);
+}
+
+// The second kernel of one entry point, whose only input is its predecessor's
+// output (a split merge after the splits): launched as a programmatic dependent
+// whatever NIB_B200_PDL says, so its CTAs wait at pdl_enter() in the
+// predecessor's tail instead of behind a launch gap. The predecessor triggers
+// its dependents only once all of its CTAs have started, so the waiting CTAs
+// never keep one of them from running.
+template <typename... KArgs, typename... Args>
+inline void launch_k_after(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                           Args&&... args) {
+  launch_k_pdl(true, kernel, grid, block, smem, st, std::forward<Args>(args)...);
 }
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
