@@ -1,6 +1,19 @@
 """Shared helpers for the parity tests."""
 
+import os
+from pathlib import Path
+
 import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def report_dir() -> Path:
+    """Where GPU tests write their measurement reports (JSON): ``$NIB_TEST_REPORT_DIR``,
+    else ``test_reports/`` at the repository root (git-ignored). Created on demand."""
+    d = Path(os.environ.get("NIB_TEST_REPORT_DIR") or (ROOT / "test_reports"))
+    d.mkdir(parents=True, exist_ok=True)
+    return d
 
 BF16 = torch.bfloat16
 

@@ -21,12 +21,12 @@ def golden():
 
 def pytest_sessionfinish(session, exitstatus):
     """Write the measured parity exceptions (tests/_util.PARITY_REPORT) to
-    gpurun_out/parity_report.json when a GPU session produced any."""
+    parity_report.json in the report directory (tests/_util.report_dir) when a
+    GPU session produced any."""
     try:
-        from tests._util import PARITY_REPORT
+        from tests._util import PARITY_REPORT, report_dir
     except ImportError:
         return
-    out = ROOT / "gpurun_out"
-    if PARITY_REPORT and out.is_dir():
+    if PARITY_REPORT:
         import json
-        (out / "parity_report.json").write_text(json.dumps(PARITY_REPORT, indent=1, sort_keys=True))
+        (report_dir() / "parity_report.json").write_text(json.dumps(PARITY_REPORT, indent=1, sort_keys=True))

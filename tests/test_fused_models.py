@@ -129,9 +129,8 @@ def test_fused_route_through_reference_models_gpu(tmp_path):
         acc[2] += float(t.pow(2).sum())
     for model, (ef, er, tt) in sums.items():
         report[model] = dict(fused_rel_err=(ef / tt) ** 0.5, reference_rel_err=(er / tt) ** 0.5)
-    out = ROOT / "gpurun_out"
-    if out.is_dir():
-        (out / "fused_models_vs_reference.json").write_text(json.dumps(report, indent=1))
+    from tests._util import report_dir
+    (report_dir() / "fused_models_vs_reference.json").write_text(json.dumps(report, indent=1))
     for model in sums:
         r = report[model]
         assert r["fused_rel_err"] <= 1.25 * r["reference_rel_err"], (model, r)

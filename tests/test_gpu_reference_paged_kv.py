@@ -14,7 +14,8 @@ namespace as this repo's binding) on the shared seeded inputs of
 * C5 head shapes (65,536 tokens into a 1,024-block cache pair; 16 sequences x
   16,384 tokens gathered): bit-identical results (sha256 of the caches and of
   the gathered rows), and both sides timed one call at a time after an L2
-  flush. The times go to ``gpurun_out/reference_paged_kv.json``.
+  flush. The times go to ``reference_paged_kv.json`` in the report directory
+  (``tests/_util.report_dir``).
 
 Skips where the library has not been built (no reference checkout at build time).
 """
@@ -88,6 +89,5 @@ def test_c5_shapes_match_and_are_timed_beside_the_reference(reference):
                                 "ours_frac_varlen": frac(gather_bytes, varlen_ms),
                                 "reference_frac": frac(gather_bytes, rt["gather_16_calls_ms"])},
         "peak_gbs": peak}
-    out = ROOT / "gpurun_out"
-    if out.is_dir():
-        (out / "reference_paged_kv.json").write_text(json.dumps(report, indent=1))
+    from tests._util import report_dir
+    (report_dir() / "reference_paged_kv.json").write_text(json.dumps(report, indent=1))
